@@ -1,0 +1,42 @@
+// kernels.h -- internal launch interface between the C ABI (api.cu) and the
+// kernel translation units.  Not part of the public boundary.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace mlpg {
+
+struct RunArgs {
+  int dt;
+  const void* X;
+  const void* W;
+  void* Y;
+  const uint8_t* xscale;
+  const uint8_t* wscale;
+  int N, K, M;
+  void* ws;          // caller workspace (may be null when none is needed)
+  size_t ws_bytes;
+  cudaStream_t stream;
+  int* dev_err;      // device error word (bounded-wait timeouts)
+  int num_sms;
+};
+
+// ---- CUDA-core split-K GEMV (thin rows; also the any-shape fallback) --------
+int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms);
+size_t gemv_workspace(int dt, int ksplit, int N, int K, int M);
+cudaError_t launch_gemv(const RunArgs& a, int ksplit);
+
+// ---- tcgen05 tensor-core GEMM --------------------------------------------------
+// bn: output tile width (128 or 256); bm is 128.
+bool tc_supported(int dt, int bn, int N, int K, int M);
+size_t tc_workspace(int dt, int bn, int N, int K, int M);
+int tc_launches(int dt);
+cudaError_t launch_tc(const RunArgs& a, int bn);
+
+// ---- peak probe -----------------------------------------------------------------
+cudaError_t launch_peak(int kind, int reps, int ctas, float* sink, int* dev_err,
+                        cudaStream_t st);
+double peak_flops_per_launch(int kind, int reps, int ctas);
+
+}  // namespace mlpg

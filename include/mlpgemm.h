@@ -1,0 +1,178 @@
+/*
+ * mlpgemm.h -- C ABI of libgemm.so, the B200 (sm_100a) MLP GEMM library.
+ *
+ *     Y[N,M] = X[N,K] @ W[K,M]          (row-major, caller-owned buffers)
+ *
+ * The reference (Anemll/fp8-mlp-metal41-bench) exposes this GEMM as Metal
+ * compute kernels named "<kernel>_<BM>x<BN>" with buffer slots X@0, W@1,
+ * Y@2, N@3, K@4, M@5 and the UE8M0 scale planes at @6/@7, dispatched one
+ * command buffer at a time by the Swift host (fp8_mlp.metal:114-461,
+ * main.swift:486-521).  Each entry point below says which part of that
+ * interface it replaces.  Plain pointers and sizes only; no C++ or torch
+ * types cross this boundary.
+ *
+ * Operand layouts (identical to the reference's buffers, main.swift:364-418):
+ *   X      fp16 | int8 | fp8 | mxfp4 : IEEE half [N,K]
+ *          i8i8                        : int8 [N,K]
+ *          f8f8 | mxfp4/a8 | mxfp4/f8  : E4M3 bytes [N,K]
+ *          f4f4 | mxfp4/a4             : E2M1, two per byte along K, low nibble = even element
+ *   W      fp16 half [K,M]; int8/i8i8 int8 [K,M]; fp8/f8f8 E4M3 [K,M];
+ *          f4f4 E2M1 [K,M] packed along M;
+ *          mxfp4, mxfp4/a4, mxfp4/a8, mxfp4/f8: E2M1 stored TRANSPOSED [M,K],
+ *          packed along K
+ *   xscale UE8M0 [N, K/32]  (mxfp4/a4, mxfp4/a8; slot @6 in the reference)
+ *   wscale UE8M0 [M, K/32]  (every mxfp4* dtype; slot @6 or @7)
+ *   Y      float32 [N,M]; int32 [N,M] for i8i8.  Y is overwritten.
+ * Layout rules (main.swift:473-476): f4f4 needs even N*K and K*M; the mxfp4
+ * family needs K % 32 == 0; mxfp4/a8 and mxfp4/f8 need K % 128 == 0.
+ *
+ * Every function returns a status code (GEMM_OK ... ) unless stated.
+ * The library allocates no device memory inside gemm_run / gemm_time:
+ * buffers (and the workspace some kernels need) come from the caller.
+ */
+#ifndef MLPGEMM_H
+#define MLPGEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (the reference's exit codes 1/2/3 keep their meaning) -- */
+#define GEMM_OK           0
+#define GEMM_ERR_ARGS     1  /* bad argument, shape or layout  (main.swift exit(1)) */
+#define GEMM_ERR_INIT     2  /* device / library initialisation (exit(2))          */
+#define GEMM_ERR_MISMATCH 3  /* result check failed (used by drivers, exit(3))      */
+#define GEMM_ERR_CUDA     4  /* CUDA runtime error                                  */
+#define GEMM_ERR_TIMEOUT  5  /* a device-side bounded wait expired                  */
+
+/* ---- dtypes: the order of `enum DType`, main.swift:85-95 ------------------ */
+#define GEMM_FP16      0
+#define GEMM_INT8      1
+#define GEMM_I8I8      2
+#define GEMM_FP8       3
+#define GEMM_F8F8      4
+#define GEMM_F4F4      5
+#define GEMM_MXFP4     6
+#define GEMM_MXFP4_A4  7
+#define GEMM_MXFP4_A8  8
+#define GEMM_MXFP4_F8  9
+#define GEMM_NUM_DTYPES 10
+
+/* ---- library / device ---------------------------------------------------- */
+
+/* Select and initialise a CUDA device, check it is sm_100 and load the
+ * kernels.  Replaces MTLCreateSystemDefaultDevice + loadLibrary
+ * (main.swift:214-244, :272-297).  Returns GEMM_ERR_INIT if no usable B200. */
+int gemm_init(int device);
+
+/* Number of visible CUDA devices (0 on a host without a GPU). */
+int gemm_device_count(void);
+
+/* Device name and architecture string ("sm_100"), the inputs of the profile
+ * slug (device.name and device.architecture.name, main.swift:320-326). */
+int gemm_device_info(int device, char *name, int name_len, char *arch, int arch_len,
+                     int *sm_count);
+
+/* Most recent error message of the calling thread ("" if none). */
+const char *gemm_last_error(void);
+
+/* Library version string. */
+const char *gemm_version(void);
+
+/* ---- dtypes and tiles ---------------------------------------------------- */
+
+/* dtype name as on the reference CLI ("fp16" ... "mxfp4/f8") and its
+ * reference kernel name ("fp16_mlp_gemm" ...), main.swift:85-111. */
+const char *gemm_dtype_name(int dtype);
+const char *gemm_kernel_name(int dtype);
+
+/* The tile list that replaces the reference's ten BMxBN threadgroup tiles
+ * (main.swift:135-143, fp8_mlp.metal:446-450).  Tensor-core tiles are named
+ * "<BM>x<BN>" (BM rows of Y per CTA, BN columns); the CUDA-core split-K
+ * kernels for thin rows are named "gemv.k<S>" (S = K splits). */
+int gemm_num_tiles(void);
+const char *gemm_tile_name(int tile);
+int gemm_tile_index(const char *name);          /* -1 if unknown */
+
+/* 1 if `tile` can run this dtype and shape, else 0. */
+int gemm_tile_supported(int dtype, int tile, int N, int K, int M);
+
+/* Built-in default tile (defaultTile, main.swift:148-154). */
+int gemm_default_tile(int dtype, int N, int K, int M);
+
+/* Layout rules of main.swift:473-476; GEMM_OK or GEMM_ERR_ARGS. */
+int gemm_check_layout(int dtype, int N, int K, int M);
+
+/* Bytes of device workspace gemm_run needs for this dtype/tile/shape
+ * (split-K partial sums and counters, the f4f4 weight transpose).  0 means
+ * no workspace.  Counters in the workspace must be zero before the first
+ * call; every kernel leaves them zero on exit. */
+size_t gemm_workspace_size(int dtype, int tile, int N, int K, int M);
+
+/* ---- memory (for callers without their own allocator) -------------------- */
+void *gemm_alloc(int device, size_t bytes);
+int gemm_free(int device, void *ptr);
+int gemm_memset(int device, void *ptr, int value, size_t bytes);
+int gemm_h2d(int device, void *dst, const void *src, size_t bytes);
+int gemm_d2h(int device, void *dst, const void *src, size_t bytes);
+/* Page-locked host memory, for end-to-end copies. */
+void *gemm_host_alloc(size_t bytes);
+int gemm_host_free(void *ptr);
+
+/* ---- compute --------------------------------------------------------------- */
+
+/* Enqueue one GEMM on `stream` (a cudaStream_t; NULL = the default stream).
+ * Replaces one dispatchThreadgroups of "<kernel>_<tile>" with the buffer
+ * bindings of main.swift:497-511.  xscale/wscale follow the slot rules of
+ * main.swift:505-510 (pass NULL where the dtype has no plane).  `workspace`
+ * must hold gemm_workspace_size() bytes (NULL if that is 0).
+ * Asynchronous: errors of the kernel itself surface at gemm_sync. */
+int gemm_run(int device, int dtype, int tile, const void *X, const void *W, void *Y,
+             int N, int K, int M, const void *xscale, const void *wscale,
+             void *workspace, size_t workspace_bytes, void *stream);
+
+/* Wait for all work on `stream` and check the device error word (timeouts of
+ * bounded waits).  The cb.waitUntilCompleted + status check of
+ * main.swift:513-518. */
+int gemm_sync(int device, void *stream);
+
+/* Time `iters` GEMMs after `warmup` untimed ones, one CUDA-event pair per
+ * iteration on an internal stream, launches queued back to back (the runOnce
+ * loop of main.swift:545-555 with GPU timestamps replaced by CUDA events).
+ * Ws / wscales are arrays of `nrot` weight copies used round-robin, so that
+ * weights smaller than L2 still stream from HBM every iteration (nrot = 1:
+ * the reference's behaviour).  If `flush` is non-NULL, `flush_bytes` of it
+ * are overwritten before every timed iteration, outside its event pair, so
+ * each timed GEMM starts with a cold L2.  ms_out receives `iters` times. */
+int gemm_time(int device, int dtype, int tile, const void *X, const void *const *Ws, void *Y,
+              int N, int K, int M, const void *xscale, const void *const *wscales, int nrot,
+              void *workspace, size_t workspace_bytes, int warmup, int iters,
+              void *flush, size_t flush_bytes, float *ms_out);
+
+/* Like gemm_time, but each iteration also copies X (and xscale) from pinned
+ * host memory before the GEMM and Y back to pinned host memory after it, all
+ * inside the timed region (end-to-end time through this C ABI). */
+int gemm_time_e2e(int device, int dtype, int tile, const void *hX, void *dX,
+                  const void *dW, void *dY, void *hY, int N, int K, int M,
+                  const void *hxscale, void *dxscale, const void *dwscale,
+                  void *workspace, size_t workspace_bytes, int warmup, int iters,
+                  float *ms_out);
+
+/* Per-launch kernel time of the dominant kernel inside gemm_time's loop, and
+ * the number of kernels one gemm_run launches (for the roofline report). */
+int gemm_launches_per_run(int dtype, int tile, int N, int K, int M);
+
+/* ---- pure-compute peak probe (tune/peak.metal + tune/peak.swift) ------------ */
+/* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4.
+ * Runs `iters` launches of a kernel that issues `reps` tcgen05.mma per CTA
+ * on operands resident in shared memory (no global traffic in the loop) and
+ * reports the median dense TFLOP/s (TOP/s for i8). */
+int gemm_peak_probe(int device, int kind, int reps, int iters, double *tflops_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MLPGEMM_H */

@@ -1,0 +1,119 @@
+"""GPU parity: libgemm.so kernels (through the C ABI) against the oracle.
+
+Every case runs one GEMM on seeded operands and compares the WHOLE output
+with the oracle's fp64 dot product of the decoded operands (int64 for
+i8i8):
+  i8i8         bit-exact
+  float dtypes max relative error <= 1e-3, where the denominator is
+               max(|ref|, 1e-2 * rms(ref)) so that outputs that cancel to
+               near zero are judged against the scale of the output.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from mlpgemm import formats as F
+from mlpgemm.data import Operands
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+
+
+def run_case(G, dtype, tile, N, K, M, mode="seeded", seed=0, ops=None):
+    ops = ops or Operands(N, K, M, mode, seed)
+    dt = F.CODE[dtype]
+    ti = G.tile_index(tile)
+    assert G.tile_supported(dt, ti, N, K, M), (dtype, tile, N, K, M)
+    X = G.DeviceBuffer(0, ops.X(dtype).nbytes).upload(ops.X(dtype))
+    W = G.DeviceBuffer(0, ops.W(dtype).nbytes).upload(ops.W(dtype))
+    xs = ops.xscale(dtype)
+    ws = ops.wscale(dtype)
+    XS = G.DeviceBuffer(0, xs.nbytes).upload(xs) if xs is not None else None
+    WS = G.DeviceBuffer(0, ws.nbytes).upload(ws) if ws is not None else None
+    Y = G.DeviceBuffer(0, N * M * 4)
+    Y.zero()
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+    G.run(0, dt, ti, X, W, Y, N, K, M, XS, WS, WSP, wsb)
+    G.sync(0)
+    out = np.empty((N, M), dtype=np.int32 if dtype == "i8i8" else np.float32)
+    Y.download(out)
+    ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), xs, ws, N, K, M)
+    return out, ref, ops
+
+
+def assert_close(dtype, out, ref):
+    if dtype == "i8i8":
+        bad = np.argwhere(out.astype(np.int64) != ref)
+        assert bad.size == 0, f"{len(bad)} mismatches, first {bad[:5].tolist()}"
+        return 0.0
+    assert np.all(np.isfinite(out))
+    rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
+    den = np.maximum(np.abs(ref), 1e-2 * rms + 1e-30)
+    rel = np.abs(out.astype(np.float64) - ref) / den
+    worst = np.unravel_index(np.argmax(rel), rel.shape)
+    assert rel.max() <= REL_TOL, f"max rel {rel.max():.3g} at {worst}: got {out[worst]} ref {ref[worst]}"
+    return float(rel.max())
+
+
+TC_DTYPES = ["fp16", "i8i8", "f8f8"]
+
+
+@pytest.mark.parametrize("dtype", TC_DTYPES)
+@pytest.mark.parametrize("tile", ["128x256", "128x128"])
+@pytest.mark.parametrize("shape", [(256, 512, 512), (200, 320, 272), (1000, 1024, 1296)])
+def test_tensor_core_tiles(gemm, dtype, tile, shape):
+    N, K, M = shape
+    out, ref, _ = run_case(gemm, dtype, tile, N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", TC_DTYPES)
+def test_tensor_core_reference_patterns(gemm, dtype):
+    # the reference's own deterministic operands (main.swift:379-390)
+    out, ref, _ = run_case(gemm, dtype, "128x256", 384, 1024, 768, mode="ref")
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", F.DTYPES)
+@pytest.mark.parametrize("tile", ["gemv.k1", "gemv.k8", "gemv.k64"])
+def test_gemv_thin_rows(gemm, dtype, tile):
+    N, K, M = 1, 1024, 1504
+    out, ref, _ = run_case(gemm, dtype, tile, N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", F.DTYPES)
+@pytest.mark.parametrize("N", [2, 5, 16])
+def test_gemv_ragged(gemm, dtype, N):
+    K = 256 if dtype in F.W_MX else 98
+    M = 50
+    out, ref, _ = run_case(gemm, dtype, "gemv.k4", N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", F.DTYPES)
+def test_suite_thin_row(gemm, dtype):
+    # the suite's thin row (N=1, K=4096, M=11008) with the default tile
+    N, K, M = 1, 4096, 11008
+    tile = gemm.tile_names()[gemm.default_tile(F.CODE[dtype], N, K, M)]
+    out, ref, _ = run_case(gemm, dtype, tile, N, K, M)
+    assert_close(dtype, out, ref)
+
+
+def test_gemv_deterministic_and_counters_reset(gemm):
+    # two calls on one workspace: identical bits (fixed reduction order) and
+    # the split-K counters are back at zero for the second call
+    a, ref, ops = run_case(gemm, "fp8", "gemv.k16", 3, 2048, 777)
+    b, _, _ = run_case(gemm, "fp8", "gemv.k16", 3, 2048, 777, ops=ops)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert_close("fp8", a, ref)
+
+
+def test_rejects_bad_layout(gemm):
+    G = gemm
+    dt = F.CODE["mxfp4/a8"]
+    with pytest.raises(G.GemmError) as e:
+        G.run(0, dt, G.tile_index("gemv.k1"), 1, 1, 1, 4, 96, 8, 1, 1)
+    assert e.value.code == G.GEMM_ERR_ARGS
