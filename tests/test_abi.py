@@ -1,0 +1,66 @@
+"""The C ABI library loads on a CPU-only host and exports every symbol that
+include/mlpgemm.h declares; host-side tables behave like the reference's."""
+import os
+import re
+
+import pytest
+
+from conftest import ROOT, golden
+from mlpgemm import formats as F
+from mlpgemm import lib as G
+
+
+def header_symbols():
+    with open(os.path.join(ROOT, "include", "mlpgemm.h")) as f:
+        text = f.read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gemm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    L = G.lib()
+    syms = header_symbols()
+    assert len(syms) >= 25
+    for s in syms:
+        assert hasattr(L, s), s
+    assert sorted(G.EXPORTS) == syms
+
+
+def test_init_fails_loudly_without_gpu():
+    if G.device_count() > 0:
+        pytest.skip("a GPU is present")
+    with pytest.raises(G.GemmError) as e:
+        G.init(0)
+    assert e.value.code == G.GEMM_ERR_INIT
+
+
+def test_dtype_and_kernel_names_match_reference():
+    L = G.lib()
+    ref = golden("reference_tables.json")["dtypes"]["values"]
+    assert [L.gemm_dtype_name(i).decode() for i in range(10)] == ref == F.DTYPES
+    assert [L.gemm_kernel_name(i).decode() for i in range(10)] == F.KERNELS
+
+
+def test_tile_table():
+    names = G.tile_names()
+    assert "128x256" in names and "128x128" in names
+    assert all(G.tile_index(n) == i for i, n in enumerate(names))
+    assert G.tile_index("64x32") == -1
+
+
+def test_layout_rules_and_tile_support():
+    L = G.lib()
+    assert L.gemm_check_layout(F.CODE["mxfp4/a8"], 4, 96, 8) == G.GEMM_ERR_ARGS
+    assert L.gemm_check_layout(F.CODE["mxfp4/a8"], 4, 128, 8) == G.GEMM_OK
+    t256 = G.tile_index("128x256")
+    assert G.tile_supported(F.CODE["i8i8"], t256, 4096, 4096, 4096)
+    assert not G.tile_supported(F.CODE["i8i8"], t256, 4096, 4100, 4096)   # TMA stride rule
+    # thin rows: the CUDA-core kernel; the default tile is a gemv tile
+    assert G.tile_names()[G.default_tile(F.CODE["int8"], 1, 4096, 11008)].startswith("gemv")
+    assert G.tile_names()[G.default_tile(F.CODE["i8i8"], 4096, 4096, 4096)] == "128x256"
+
+
+def test_workspace_sizes():
+    t = G.tile_index("gemv.k32")
+    assert G.workspace_size(F.CODE["int8"], t, 1, 4096, 11008) == 65536 + 32 * 11008 * 4
+    assert G.workspace_size(F.CODE["int8"], G.tile_index("gemv.k1"), 1, 4096, 11008) == 0
