@@ -171,6 +171,8 @@ int validate(int device, int dt, int tile, const void* X, const void* W, void* Y
 
 }  // namespace
 
+void mlpg::set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+
 extern "C" {
 
 const char* gemm_version(void) { return "mlpgemm 0.1 (sm_100a tcgen05)"; }

@@ -34,6 +34,9 @@ size_t tc_workspace(int dt, int bn, int N, int K, int M);
 int tc_launches(int dt);
 cudaError_t launch_tc(const RunArgs& a, int bn);
 
+// Record a message for gemm_last_error() (defined in api.cu).
+void set_last_error(const char* msg);
+
 // ---- peak probe -----------------------------------------------------------------
 cudaError_t launch_peak(int kind, int reps, int ctas, float* sink, int* dev_err,
                         cudaStream_t st);

@@ -22,7 +22,7 @@ EXPORTS = [
     "gemm_tile_index", "gemm_tile_supported", "gemm_default_tile", "gemm_check_layout",
     "gemm_workspace_size", "gemm_alloc", "gemm_free", "gemm_memset", "gemm_h2d", "gemm_d2h",
     "gemm_host_alloc", "gemm_host_free", "gemm_run", "gemm_sync", "gemm_time",
-    "gemm_time_e2e", "gemm_launches_per_run", "gemm_peak_probe",
+    "gemm_time_e2e", "gemm_launches_per_run", "gemm_peak_probe", "gemm_run_noalloc",
 ]
 
 
@@ -78,6 +78,8 @@ def _declare(L):
                                   ctypes.POINTER(ctypes.c_float)]),
         "gemm_launches_per_run": (c_int, [c_int, c_int, c_int, c_int, c_int]),
         "gemm_peak_probe": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
+        "gemm_run_noalloc": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp,
+                                     vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -220,6 +222,15 @@ def run(device, dtype, tile, X, W, Y, N, K, M, xscale=None, wscale=None, workspa
     check(lib().gemm_run(device, dtype, tile, as_ptr(X), as_ptr(W), as_ptr(Y), N, K, M,
                          as_ptr(xscale), as_ptr(wscale), as_ptr(workspace), int(workspace_bytes),
                          as_ptr(stream)), "gemm_run")
+
+
+def run_noalloc(device, dtype, ksplit, X, W, Y, N, K, M, xscale=None, wscale=None,
+                stream=None) -> None:
+    """Thin-row GEMM whose split-K scratch is the library's fixed device array
+    (no allocation by the library or the caller; see gemm_run_noalloc)."""
+    check(lib().gemm_run_noalloc(device, dtype, ksplit, as_ptr(X), as_ptr(W), as_ptr(Y), N, K, M,
+                                 as_ptr(xscale), as_ptr(wscale), as_ptr(stream)),
+          "gemm_run_noalloc")
 
 
 def sync(device: int = 0, stream=None) -> None:

@@ -165,6 +165,23 @@ int gemm_time_e2e(int device, int dtype, int tile, const void *hX, void *dX,
  * the number of kernels one gemm_run launches (for the roofline report). */
 int gemm_launches_per_run(int dtype, int tile, int N, int K, int M);
 
+/* ---- thin rows without any allocation ------------------------------------------
+ * No counterpart in the reference (whose Metal host allocates freely).
+ * For callers that may not allocate device memory and can only pass their
+ * own inputs and outputs: plugin hosts and serving loops that own every
+ * device allocation and forbid new ones after start-up, and bindings that
+ * expose no allocator.  Same operands, layouts and results as gemm_run with
+ * a "gemv.k<ksplit>" tile (N <= 16; ksplit <= 0 picks one), but the split-K
+ * scratch lives in a fixed 8 MiB device array inside the library, held on
+ * every GPU that loads the library until the process exits.  Requests whose
+ * scratch (64 KiB of counters + ksplit*N*M*4 bytes) exceeds 8 MiB return
+ * GEMM_ERR_ARGS.  The first call on a device looks up the array's address on
+ * that device; make it before any stream capture.  All calls share the array
+ * (each clears its counters first): calls that overlap on the GPU race and
+ * must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
+int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const void *W, void *Y,
+                     int N, int K, int M, const void *xscale, const void *wscale, void *stream);
+
 /* ---- pure-compute peak probe (tune/peak.metal + tune/peak.swift) ------------ */
 /* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4.
  * Runs `iters` launches of a kernel that issues `reps` tcgen05.mma per CTA
