@@ -9,7 +9,9 @@
 //   warp 1      TMEM allocator + single-thread MMA issuer: tcgen05.mma into a
 //               double-buffered TMEM accumulator, tcgen05.commit frees ring
 //               slots ("empty") and hands finished tiles to the epilogue
-//   warp 2      (block-scaled kinds) UE8M0 scale-factor stager
+//   warp 2      block-scaled kinds only: stages the UE8M0 scale factors of
+//               each ring slot in shared memory in the layout tcgen05.cp
+//               copies to TMEM (32 rows x 16 bytes per MMA and operand)
 //   warps 4-7   epilogue: tcgen05.ld TMEM -> registers -> Y, one TMEM lane
 //               quadrant (32 output rows) per warp
 //
@@ -17,6 +19,19 @@
 // Y by BN (128 or 256) columns.  X is always K-major.  W is MN-major for
 // the [K,M] dtypes (fp16, i8i8, f8f8: the instruction descriptor's
 // "transpose B" bit) and K-major for the [M,K] mxfp4 family.
+//
+// Kinds per dtype:
+//   fp16                 kind::f16       F16 x F16 -> F32
+//   i8i8                 kind::i8        S8 x S8 -> S32 (exact)
+//   f8f8                 kind::f8f6f4    E4M3 x E4M3 -> F32
+//   mxfp4/a4             kind::mxf4      E2M1 x E2M1, UE8M0 per 32 on both
+//   f4f4                 kind::mxf4      E2M1 x E2M1 with unit scales (127);
+//                                        W [K,M] is first transposed to
+//                                        [M,K] into the workspace (the MMA
+//                                        needs 4-bit operands K-major)
+//   mxfp4/a8, mxfp4/f8   kind::mxf8f6f4  E4M3 x E2M1, UE8M0 per 32; TMA
+//                                        unpacks the E2M1 weights into
+//                                        8-bit containers (16U4_ALIGN16B)
 //
 // Every mbarrier wait is bounded (ptx.cuh); on expiry the kernel records
 // an error word, lets in-flight TMA copies land, frees TMEM and returns.
@@ -37,49 +52,86 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kThreads = 256;
 constexpr int kRowBytes = 128;   // bytes of K per operand row per stage (one swizzle row)
+constexpr int kSfChunk = 512;    // one 32 x 16-byte scale-factor block (one tcgen05.cp)
 
 // Per-dtype kernel traits.
+//   a_bits/b_bits   bits per element as stored in shared memory per K element
+//                   (E2M1 for kind::mxf8f6f4 is unpacked to 8 bits by TMA)
+//   nsf             UE8M0 scale factors per row per MMA (0 = unscaled kind)
+//   x_plane/w_plane the dtype reads an X / W scale plane (else the scale is 1)
 template <int DT>
 struct Traits;
 
 template <>
 struct Traits<kFP16> {
-  static constexpr int kind = kKindF16;
-  static constexpr int a_bits = 16, b_bits = 16;
-  static constexpr bool b_mn = true, out_int = false, scaled = false;
+  static constexpr int kind = kKindF16, a_bits = 16, b_bits = 16, nsf = 0;
+  static constexpr bool b_mn = true, x_plane = false, w_plane = false, b_unpack4 = false;
   static constexpr uint32_t a_fmt = 0, b_fmt = 0, c_fmt = 1;  // F16, F16 -> F32
 };
 template <>
 struct Traits<kI8I8> {
-  static constexpr int kind = kKindI8;
-  static constexpr int a_bits = 8, b_bits = 8;
-  static constexpr bool b_mn = true, out_int = true, scaled = false;
+  static constexpr int kind = kKindI8, a_bits = 8, b_bits = 8, nsf = 0;
+  static constexpr bool b_mn = true, x_plane = false, w_plane = false, b_unpack4 = false;
   static constexpr uint32_t a_fmt = 1, b_fmt = 1, c_fmt = 2;  // S8, S8 -> S32
 };
 template <>
 struct Traits<kF8F8> {
-  static constexpr int kind = kKindF8F6F4;
-  static constexpr int a_bits = 8, b_bits = 8;
-  static constexpr bool b_mn = true, out_int = false, scaled = false;
+  static constexpr int kind = kKindF8F6F4, a_bits = 8, b_bits = 8, nsf = 0;
+  static constexpr bool b_mn = true, x_plane = false, w_plane = false, b_unpack4 = false;
   static constexpr uint32_t a_fmt = 0, b_fmt = 0, c_fmt = 1;  // E4M3, E4M3 -> F32
+};
+template <>
+struct Traits<kMX4X4> {
+  static constexpr int kind = kKindMxF4, a_bits = 4, b_bits = 4, nsf = 2;
+  static constexpr bool b_mn = false, x_plane = true, w_plane = true, b_unpack4 = false;
+  static constexpr uint32_t a_fmt = 1, b_fmt = 1, c_fmt = 1;  // E2M1 (mxf4), E2M1
+};
+template <>
+struct Traits<kF4F4> {
+  static constexpr int kind = kKindMxF4, a_bits = 4, b_bits = 4, nsf = 2;
+  static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = false;
+  static constexpr uint32_t a_fmt = 1, b_fmt = 1, c_fmt = 1;
+};
+template <>
+struct Traits<kMX8X4> {
+  static constexpr int kind = kKindMxF8F6F4, a_bits = 8, b_bits = 8, nsf = 1;
+  static constexpr bool b_mn = false, x_plane = true, w_plane = true, b_unpack4 = true;
+  static constexpr uint32_t a_fmt = 0, b_fmt = 5, c_fmt = 1;  // E4M3, E2M1
+};
+template <>
+struct Traits<kF8X4> {
+  static constexpr int kind = kKindMxF8F6F4, a_bits = 8, b_bits = 8, nsf = 1;
+  static constexpr bool b_mn = false, x_plane = false, w_plane = true, b_unpack4 = true;
+  static constexpr uint32_t a_fmt = 0, b_fmt = 5, c_fmt = 1;
 };
 
 struct TcParams {
   void* Y;
+  const uint8_t* xscale;   // [N, K/32] UE8M0 or null (scale 1)
+  const uint8_t* wscale;   // [M, K/32] UE8M0 or null (scale 1)
   int N, K, M;
   int tiles_m, tiles_n, num_kb;
   int* dev_err;
 };
 
+constexpr uint32_t pow2_cols(int c) {
+  return c <= 32 ? 32u : c <= 64 ? 64u : c <= 128 ? 128u : c <= 256 ? 256u : 512u;
+}
+
 template <int DT, int BN, int STAGES>
 struct Cfg {
   using T = Traits<DT>;
+  static constexpr bool SCALED = T::nsf > 0;
   static constexpr int A_BYTES = kBM * kRowBytes;            // 16 KB
   static constexpr int B_BYTES = BN * kRowBytes;             // 16 / 32 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // transaction bytes per stage: the 16U4_ALIGN16B load counts the packed
+  // 4-bit source bytes (half of what it writes to shared memory)
+  static constexpr int STAGE_TX = A_BYTES + (T::b_unpack4 ? B_BYTES / 2 : B_BYTES);
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;  // elements
   static constexpr int MMA_K_BYTES = 32;                     // K bytes per tcgen05.mma
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;  // 4
+  static constexpr int KBLK_PER_STAGE = K_PER_STAGE / 32;    // UE8M0 blocks per stage
   // MN-major B: one TMA box is K_PER_STAGE rows x 128 bytes of MN
   static constexpr int B_BOX_MN = kRowBytes * 8 / T::b_bits; // MN elements per box
   static constexpr int B_BOXES = T::b_mn ? BN / B_BOX_MN : 1;
@@ -88,15 +140,31 @@ struct Cfg {
   static constexpr uint32_t B_LBO = T::b_mn ? (uint32_t)B_BOX_BYTES : 16u;
   static constexpr uint32_t B_ADV = T::b_mn ? (uint32_t)(MMA_K_BYTES * 8 / T::b_bits) * kRowBytes
                                             : (uint32_t)MMA_K_BYTES;
+  // scale factors: per stage and MMA one 512-byte block for A, BN/128 for B
+  static constexpr int SF_B_CHUNKS = BN / 128;
+  static constexpr int SF_A_BYTES = SCALED ? MMAS_PER_STAGE * kSfChunk : 0;
+  static constexpr int SF_B_BYTES = SCALED ? MMAS_PER_STAGE * SF_B_CHUNKS * kSfChunk : 0;
+  static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
+  static constexpr int SF_OFF = STAGES * STAGE_BYTES;
+  // TMEM: [0, 2*BN) accumulators; then per stage 4 columns per MMA for A and
+  // 4*BN/128 per MMA for B (one 32-bit column per 32 rows, byte s = block s)
   static constexpr int ACC_COLS = BN;
-  static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SF_COL0 = 2 * BN;
+  static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
+  static constexpr int SF_COLS_STAGE = SCALED ? MMAS_PER_STAGE * (SF_COLS_A + SF_COLS_B) : 0;
+  static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN + STAGES * SF_COLS_STAGE);
+  static constexpr int BAR_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
   static constexpr uint32_t IDESC =
-      (T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | (0u << 15) |
-      ((T::b_mn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+      SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
+                ((uint32_t)(kBM >> 4) << 24))
+             : ((T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) |
+                ((T::b_mn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                ((uint32_t)(kBM >> 4) << 24));
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
   static_assert(!T::b_mn || BN % B_BOX_MN == 0, "MN-major B tile must be whole swizzle atoms");
+  static_assert(2 * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 struct Bars {
@@ -111,6 +179,34 @@ struct Bars {
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int& tn) {
   tm = tile % tiles_m;
   tn = tile / tiles_m;
+}
+
+// Scale bytes of one row for the `nb` k-blocks starting at kblk0 (127 = 1.0
+// outside the matrix or without a plane).
+template <int NB>
+__device__ __forceinline__ void load_row_scales(const uint8_t* plane, int row, int rows, int kbpr,
+                                                int kblk0, uint8_t (&s)[NB]) {
+  if (plane == nullptr || row >= rows) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) s[i] = 127;
+    return;
+  }
+  const uint8_t* p = plane + (size_t)row * kbpr + kblk0;
+  const bool full = kblk0 + NB <= kbpr;
+  if (full && (reinterpret_cast<uintptr_t>(p) % NB) == 0) {
+    if constexpr (NB == 4) {
+      const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(p));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i] = (uint8_t)(v >> (8 * i));
+    } else {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[i] = (uint8_t)(v.x >> (8 * i)), s[4 + i] = (uint8_t)(v.y >> (8 * i));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NB; ++i) s[i] = (kblk0 + i < kbpr) ? __ldg(p + i) : (uint8_t)127;
+  }
 }
 
 template <int DT, int BN, int STAGES>
@@ -131,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->full[s], C::SCALED ? 2 : 1);   // producer (+ scale stager)
       mbar_init(&bars->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -166,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x100 + stage)) { ok = false; break; }
         unsigned char* a_dst = smem + stage * C::STAGE_BYTES;
         unsigned char* b_dst = a_dst + C::A_BYTES;
-        mbar_arrive_expect_tx(&bars->full[stage], C::STAGE_BYTES);
+        mbar_arrive_expect_tx(&bars->full[stage], C::STAGE_TX);
         // A tile: x in elements of the map (bytes for 8/4-bit maps)
         tma_load_2d(a_dst, &tmA, &bars->full[stage], kb * (T::a_bits == 16 ? C::K_PER_STAGE : kRowBytes),
                     tm * kBM);
@@ -176,7 +272,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(b_dst + j * C::B_BOX_BYTES, &tmB, &bars->full[stage],
                         tn * BN + j * C::B_BOX_MN, kb * C::K_PER_STAGE);
         } else {
-          tma_load_2d(b_dst, &tmB, &bars->full[stage], kb * kRowBytes, tn * BN);
+          // K-major B; x counts 4-bit elements for the unpacking map, bytes otherwise
+          tma_load_2d(b_dst, &tmB, &bars->full[stage], T::b_unpack4 ? kb * C::K_PER_STAGE : kb * kRowBytes,
+                      tn * BN);
         }
         filled[stage] = true;
         filled_parity[stage] = phase;
@@ -209,17 +307,97 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
         const uint32_t b_addr = a_addr + C::A_BYTES;
+        if constexpr (C::SCALED) {
+          const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+          const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
-        for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
-          const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
-          const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
-          tc_mma<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            const uint32_t sfa_t = sf_tmem + kk * (C::SF_COLS_A + C::SF_COLS_B);
+            const uint32_t sfb_t = sfa_t + C::SF_COLS_A;
+            tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(sf_smem + kk * kSfChunk, 0, 128));
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_32x128b_warpx4(sfb_t + 4 * c,
+                                   sdesc_plain(sf_smem + C::SF_A_BYTES + (kk * C::SF_B_CHUNKS + c) * kSfChunk, 0, 128));
+            const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+            tc_mma_bs<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u, sfa_t, sfb_t);
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+            tc_mma<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
         }
         tc_commit(&bars->empty[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
       if (!ok) break;
       tc_commit(&bars->acc_full[buf]);
+    }
+  } else if (warp == 2 && C::SCALED) {
+    // ------------------------ scale-factor stager ------------------------------
+    // For MMA kk of a stage, row r = r0 + 32*j of the operand tile: byte
+    // (16*r0 + 4*j + s) of its 512-byte block holds the scale of k-block
+    // kk*nsf + s; tcgen05.cp 32x128b.warpx4 puts row r0's 16 bytes into TMEM
+    // lane r0 (replicated to all four lane quadrants), 32-bit column j.
+    constexpr int NB = C::KBLK_PER_STAGE;   // 4 (mxf8f6f4) or 8 (mxf4)
+    const int kbpr = p.K / 32;
+    uint32_t stage = 0, phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      bool ok = true;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const bool got = mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x500 + stage);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        unsigned char* sf = smem + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+        const int kblk0 = kb * NB;
+        // A (X rows of this tile)
+        {
+          uint8_t s[4][NB];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            load_row_scales<NB>(T::x_plane ? p.xscale : nullptr, tm * kBM + lane + 32 * j, p.N, kbpr, kblk0, s[j]);
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              w[j] = s[j][kk * T::nsf];
+              if constexpr (T::nsf == 2) w[j] |= (uint32_t)s[j][kk * T::nsf + 1] << 8;
+            }
+            *reinterpret_cast<uint4*>(sf + kk * kSfChunk + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        // B (W rows = output columns of this tile)
+#pragma unroll
+        for (int c = 0; c < C::SF_B_CHUNKS; ++c) {
+          uint8_t s[4][NB];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            load_row_scales<NB>(T::w_plane ? p.wscale : nullptr, tn * BN + c * 128 + lane + 32 * j, p.M, kbpr,
+                                kblk0, s[j]);
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              w[j] = s[j][kk * T::nsf];
+              if constexpr (T::nsf == 2) w[j] |= (uint32_t)s[j][kk * T::nsf + 1] << 8;
+            }
+            *reinterpret_cast<uint4*>(sf + C::SF_A_BYTES + (kk * C::SF_B_CHUNKS + c) * kSfChunk + lane * 16) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        fence_proxy_async_smem();   // generic-proxy writes -> visible to tcgen05.cp
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->full[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
     }
   } else if (warp >= 4) {
     // ------------------------------ epilogue ----------------------------------
@@ -273,6 +451,435 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------
+// f4f4: W [K,M] packed along M -> Wt [M,K] packed along K (the 4-bit MMA
+// operands must be K-major).  One CTA transposes a 64 (K) x 256 (M) nibble
+// tile through shared memory; each thread assembles 32 nibbles of one output
+// row (16 bytes) and stores them with one 16-byte store.
+// ----------------------------------------------------------------------------
+constexpr int kTrK = 64, kTrM = 256;
+
+__global__ void __launch_bounds__(256) transpose_fp4_kernel(const uint8_t* __restrict__ W,
+                                                            uint8_t* __restrict__ Wt, int K, int M) {
+  __shared__ __align__(16) uint8_t tile[kTrK][kTrM / 2];   // 64 rows x 128 bytes
+  const int k0 = blockIdx.y * kTrK, m0 = blockIdx.x * kTrM;
+  const int t = threadIdx.x;
+  const size_t row_bytes = (size_t)M / 2;                    // M is even
+  // load: 64 rows x 8 uint4
+  for (int i = t; i < kTrK * 8; i += 256) {
+    const int r = i >> 3, c = i & 7;
+    const int k = k0 + r;
+    const int mb = m0 / 2 + c * 16;                          // byte column
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (k < K) {
+      const uint8_t* src = W + (size_t)k * row_bytes + mb;
+      if (mb + 16 <= (int)row_bytes && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v = __ldg(reinterpret_cast<const uint4*>(src));
+      } else {
+        uint8_t b[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) b[j] = (mb + j < (int)row_bytes) ? src[j] : 0;
+        v = *reinterpret_cast<uint4*>(b);
+      }
+    }
+    *reinterpret_cast<uint4*>(&tile[r][c * 16]) = v;
+  }
+  __syncthreads();
+  // store: 256 output rows x 2 halves of 32 nibbles
+  for (int i = t; i < kTrM * 2; i += 256) {
+    const int mr = i >> 1, h = i & 1;
+    const int m = m0 + mr;
+    const int kk0 = h * 32;
+    if (m >= M || k0 + kk0 >= K) continue;
+    const int byte = mr >> 1, hi = mr & 1;
+    uint32_t o[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t nib = (tile[kk0 + j][byte] >> (hi * 4)) & 0xFu;
+      o[j >> 3] |= nib << ((j & 7) * 4);
+    }
+    uint8_t* dst = Wt + (size_t)m * (K / 2) + (k0 + kk0) / 2;
+    if (k0 + kk0 + 32 <= K) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(o);
+      for (int j = 0; j < (K - k0 - kk0) / 2; ++j) dst[j] = b[j];
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// A16 widen kernel: fp16 activations x int8 / E4M3 / MXFP4 weights.
+//
+// The reference's W8A16 and MXFP4 (A16) kernels feed a half x {int8, E4M3,
+// E2M1 + UE8M0} matmul2d (fp8_mlp.metal:127-164, :199-276).  Here the weights
+// stay low-bit in HBM and shared memory: TMA brings the raw W tile of each
+// stage into a staging buffer, four converter warps widen it exactly to f16
+// straight into the 128-byte-swizzled UMMA layout, and the MMA runs
+// kind::f16 (F16 x F16 -> F32).  Warps: 0 TMA, 1 MMA, 4-7 epilogue, 8-11
+// converters (384 threads).
+//
+// Exactness: int8 -> f16 (|v| <= 128) and E4M3 -> f16 (cvt.rn.f16x2.e4m3x2)
+// are exact.  E2M1 * 2^(s-127) is an f16 value only for s in [104, 140]; a
+// pre-pass finds for every weight row m an exponent offset c_m that moves
+// the row's scales into that window (0 for ordinary planes), the converters
+// widen E2M1 * 2^(s-127-c_m) and the epilogue multiplies column m by 2^c_m.
+// ----------------------------------------------------------------------------
+constexpr int kWThreads = 384;
+
+template <int DT>
+struct WTraits {
+  static constexpr bool mx = (DT == kMXFP4);
+  static constexpr bool b_mn = !mx;   // int8 / E4M3 W is [K,M]
+};
+
+template <int DT, int BN, int STAGES>
+struct WCfg {
+  using WT = WTraits<DT>;
+  static constexpr int A_BYTES = kBM * kRowBytes;            // 128 rows x 64 halfs
+  static constexpr int B_BYTES = BN * kRowBytes;             // widened f16 tile
+  static constexpr int K_PER_STAGE = 64;
+  static constexpr int RAW_BYTES = WT::mx ? BN * 32 : K_PER_STAGE * BN;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + RAW_BYTES;
+  static constexpr int STAGE_TX = A_BYTES + RAW_BYTES;
+  static constexpr int MMAS_PER_STAGE = 4;                   // K = 16 each
+  static constexpr uint32_t B_LBO = WT::b_mn ? 64u * kRowBytes : 16u;
+  static constexpr uint32_t B_ADV = WT::b_mn ? 16u * kRowBytes : 32u;
+  static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN);
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((WT::b_mn ? 1u : 0u) << 16) |
+                                    ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+  static_assert(STAGE_BYTES % 1024 == 0, "swizzle atoms need 1 KB alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+struct WBars {
+  uint64_t full[8];
+  uint64_t conv[8];
+  uint64_t empty[8];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct WParams {
+  void* Y;
+  const uint8_t* wscale;     // mxfp4: [M, K/32]
+  const int8_t* col_exp;     // mxfp4: per-row exponent offsets c_m (from the pre-pass)
+  int N, K, M;
+  int tiles_m, tiles_n, num_kb;
+  int* dev_err;
+};
+
+// f16 multiplier 2^e for the E2M1 widening (e clamped to the f16 range).
+__device__ __forceinline__ uint32_t f16x2_pow2(int e) {
+  uint32_t h;
+  if (e >= -14) h = (uint32_t)(min(e, 15) + 15) << 10;
+  else if (e >= -24) h = 1u << (e + 24);
+  else h = 0;
+  return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// 8 int8 (two words) -> 8 f16: bias to unsigned, place each byte under the
+// exponent of 1024 (0x64xx = 1024 + byte), subtract 1152 (= 1024 + 128).
+__device__ __forceinline__ uint4 widen_i8x8(uint2 v) {
+  const uint32_t a = v.x ^ 0x80808080u, b = v.y ^ 0x80808080u;
+  const uint32_t k = 0x64806480u;   // 1152.0 in both halves
+  uint4 o;
+  o.x = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4140), k);
+  o.y = hsub2_u32(__byte_perm(a, 0x64646464u, 0x4342), k);
+  o.z = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4140), k);
+  o.w = hsub2_u32(__byte_perm(b, 0x64646464u, 0x4342), k);
+  return o;
+}
+
+__device__ __forceinline__ uint32_t cvt_e4m3x2(uint32_t two_bytes) {
+  uint32_t d;
+  const unsigned short h = (unsigned short)two_bytes;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(h));
+  return d;
+}
+
+__device__ __forceinline__ uint4 widen_e4m3x8(uint2 v) {
+  uint4 o;
+  o.x = cvt_e4m3x2(v.x);
+  o.y = cvt_e4m3x2(v.x >> 16);
+  o.z = cvt_e4m3x2(v.y);
+  o.w = cvt_e4m3x2(v.y >> 16);
+  return o;
+}
+
+// 8 E2M1 (one word, low nibble first) -> 8 f16, times the f16x2 multiplier.
+__device__ __forceinline__ uint4 widen_e2m1x8(uint32_t w, uint32_t mul) {
+  uint32_t h0, h1, h2, h3;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+      : "r"(w));
+  return make_uint4(hmul2_u32(h0, mul), hmul2_u32(h1, mul), hmul2_u32(h2, mul), hmul2_u32(h3, mul));
+}
+
+// Per weight row: the exponent offset c_m that brings the row's UE8M0 scales
+// into the window where E2M1 * 2^(s-127-c_m) is an exact f16 (s in [104,140]).
+__global__ void __launch_bounds__(256) mx_row_exp_kernel(const uint8_t* __restrict__ wscale, int M,
+                                                         int kbpr, int8_t* __restrict__ out) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  int mn = 255, mx = 0;
+  for (int i = lane; i < kbpr; i += 32) {
+    const int s = wscale[(size_t)row * kbpr + i];
+    mn = min(mn, s);
+    mx = max(mx, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  int c = 0;
+  if (mx > 140) c = mx - 140;
+  else if (mn < 104) c = max(mn - 104, mx - 140);
+  if (lane == 0) out[row] = (int8_t)c;
+}
+
+template <int DT, int BN, int STAGES>
+__global__ void __launch_bounds__(kWThreads, 1)
+    tc_widen_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmR,
+                    WParams p) {
+  using C = WCfg<DT, BN, STAGES>;
+  using WT = typename C::WT;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  WBars* bars = reinterpret_cast<WBars*>(smem + C::BAR_OFF);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  AbortCtl ctl{p.dev_err, &bars->abort_flag};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->conv[s], 4);      // one arrival per converter warp
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 4 * 32);
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmR);
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    uint32_t stage = 0, phase = 0;
+    uint32_t filled_parity[8];
+    bool filled[8];
+    for (int s = 0; s < STAGES; ++s) filled[s] = false, filled_parity[s] = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x100 + stage)) { ok = false; break; }
+        unsigned char* base = smem + stage * C::STAGE_BYTES;
+        mbar_arrive_expect_tx(&bars->full[stage], C::STAGE_TX);
+        tma_load_2d(base, &tmA, &bars->full[stage], kb * C::K_PER_STAGE, tm * kBM);
+        unsigned char* raw = base + C::A_BYTES + C::B_BYTES;
+        if constexpr (WT::mx) tma_load_2d(raw, &tmR, &bars->full[stage], kb * 32, tn * BN);
+        else tma_load_2d(raw, &tmR, &bars->full[stage], tn * BN, kb * C::K_PER_STAGE);
+        filled[stage] = true;
+        filled_parity[stage] = phase;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    if (!ok) {
+      for (int s = 0; s < STAGES; ++s) {
+        if (!filled[s]) continue;
+        const uint32_t a = smem_u32(&bars->full[s]);
+        const unsigned long long t0 = global_ns();
+        while (!mbar_try_wait(a, filled_parity[s]) && global_ns() - t0 < kWaitTimeoutNs) {}
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------ MMA issuer --------------------------------
+    uint32_t stage = 0, phase = 0;
+    int local = 0;
+    bool ok = true;
+    const uint32_t smem_base = smem_u32(smem);
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      if (!mbar_wait(&bars->acc_empty[buf], acc_par ^ 1u, ctl, 0x200 + buf)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x300 + stage) ||
+            !mbar_wait(&bars->conv[stage], phase, ctl, 0x600 + stage)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
+        const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+          const uint64_t adesc = sdesc_sw128(a_addr + kk * 32, 16, 1024);
+          const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+          tc_mma<kKindF16>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+        }
+        tc_commit(&bars->empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      tc_commit(&bars->acc_full[buf]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------ converters --------------------------------
+    const int ct = threadIdx.x - 256;   // 0..127
+    const int kbpr = p.K / 32;
+    uint32_t stage = 0, phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      (void)tm;
+      bool ok = true;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const bool got = mbar_wait(&bars->full[stage], phase, ctl, 0x700 + stage);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        unsigned char* bconv = smem + stage * C::STAGE_BYTES + C::A_BYTES;
+        const unsigned char* raw = bconv + C::B_BYTES;
+        if constexpr (WT::mx) {
+          // row n: 32 raw bytes (64 E2M1) -> 8 swizzled 16-byte chunks of f16
+#pragma unroll
+          for (int r = 0; r < BN / 128; ++r) {
+            const int n = ct + 128 * r;
+            const int m = tn * BN + n;
+            uint32_t mul0 = 0, mul1 = 0;
+            if (m < p.M) {
+              const int c_m = p.col_exp[m];
+              const uint8_t* sp = p.wscale + (size_t)m * kbpr + kb * 2;
+              const int s0 = __ldg(sp);
+              const int s1 = (kb * 2 + 1 < kbpr) ? __ldg(sp + 1) : 127;
+              mul0 = f16x2_pow2(s0 - 127 - c_m);
+              mul1 = f16x2_pow2(s1 - 127 - c_m);
+            }
+            const uint4 w0 = *reinterpret_cast<const uint4*>(raw + n * 32);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(raw + n * 32 + 16);
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            unsigned char* row = bconv + n * kRowBytes;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              const uint4 h = widen_e2m1x8(words[c], c < 4 ? mul0 : mul1);
+              *reinterpret_cast<uint4*>(row + ((c ^ (n & 7)) << 4)) = h;
+            }
+          }
+        } else {
+          // [64 K rows][BN] bytes -> BN/64 boxes of [64 K rows][128 B] f16
+          constexpr int CHUNKS = C::K_PER_STAGE * BN / 8;
+          constexpr int JB = BN / 64;
+#pragma unroll 4
+          for (int i = ct; i < CHUNKS; i += 128) {
+            const int c = i & 7, rest = i >> 3;
+            const int j = rest % JB, k = rest / JB;
+            const uint2 v = *reinterpret_cast<const uint2*>(raw + k * BN + j * 64 + c * 8);
+            const uint4 h = (DT == kINT8) ? widen_i8x8(v) : widen_e4m3x8(v);
+            *reinterpret_cast<uint4*>(bconv + j * (64 * kRowBytes) + k * kRowBytes + ((c ^ (k & 7)) << 4)) = h;
+          }
+        }
+        fence_proxy_async_smem();   // generic-proxy writes -> visible to tcgen05.mma
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->conv[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------ epilogue ----------------------------------
+    const int q = warp - 4;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      const int buf = local & 1;
+      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const bool got = mbar_wait(&bars->acc_full[buf], acc_par, ctl, 0x400 + buf);
+      if (!__all_sync(0xffffffffu, got)) break;
+      __syncwarp();
+      tc_fence_after();
+      const int row = tm * kBM + q * 32 + lane;
+      const int col0 = tn * BN;
+      const bool row_ok = row < p.N;
+      float* yrow = reinterpret_cast<float*>(p.Y) + (size_t)row * p.M;
+      const bool vec_ok = (p.M % 4) == 0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), r);
+        tmem_ld_wait();
+        const int cb = col0 + c * 32;
+        float v[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(r[t]);
+        if constexpr (WT::mx) {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            const int m = cb + t;
+            const int e = (m < p.M) ? p.col_exp[m] : 0;
+            if (e) v[t] *= __int_as_float((e + 127) << 23);   // exact power of two
+          }
+        }
+        if (row_ok) {
+          if (vec_ok && cb + 32 <= p.M) {
+            float4* dst = reinterpret_cast<float4*>(yrow + cb);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) dst[t] = make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (cb + t < p.M) yrow[cb + t] = v[t];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------------
 // host side: tensor maps through the driver entry point (no libcuda link)
 // ----------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -293,47 +900,74 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D row-major map: `inner` elements per row (contiguous), `outer` rows.
-bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType ty, int elem_bytes,
-              uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle sw) {
+// 2-D row-major map: `inner` elements per row (contiguous), `outer` rows,
+// `row_bytes` between rows.
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType ty, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * (uint64_t)elem_bytes};
+  cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, ty, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Same, without swizzle (raw weight tiles read by the converter warps).
+bool make_map_plain(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
 }
 
 template <int DT, int BN, int STAGES>
-cudaError_t launch_cfg(const RunArgs& a) {
+cudaError_t launch_cfg(const RunArgs& a, const void* W) {
   using C = Cfg<DT, BN, STAGES>;
   using T = typename C::T;
   CUtensorMap tmA, tmB;
   const CUtensorMapDataType ty8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok;
   if constexpr (T::a_bits == 16) {
-    ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)a.K, (uint64_t)a.N,
-                  C::K_PER_STAGE, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N,
+                  (uint64_t)a.K * 2, C::K_PER_STAGE, kBM);
   } else {
     const uint64_t row_bytes = (uint64_t)a.K * T::a_bits / 8;
-    ok = make_map(&tmA, a.X, ty8, 1, row_bytes, (uint64_t)a.N, kRowBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = make_map(&tmA, a.X, ty8, row_bytes, (uint64_t)a.N, row_bytes, kRowBytes, kBM);
   }
   if (!ok) return cudaErrorInvalidValue;
   if constexpr (T::b_mn) {
     const int es = T::b_bits / 8;
-    ok = make_map(&tmB, a.W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, es, (uint64_t)a.M,
-                  (uint64_t)a.K, C::B_BOX_MN, C::K_PER_STAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = make_map(&tmB, W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, (uint64_t)a.M, (uint64_t)a.K,
+                  (uint64_t)a.M * es, C::B_BOX_MN, C::K_PER_STAGE);
+  } else if constexpr (T::b_unpack4) {
+    // packed E2M1 [M,K] -> 8-bit containers in shared memory (16 values + 8 bytes gap)
+    ok = make_map(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.M,
+                  (uint64_t)a.K / 2, 128, BN);
   } else {
     const uint64_t row_bytes = (uint64_t)a.K * T::b_bits / 8;
-    ok = make_map(&tmB, a.W, ty8, 1, row_bytes, (uint64_t)a.M, kRowBytes, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = make_map(&tmB, W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, BN);
   }
   if (!ok) return cudaErrorInvalidValue;
 
   TcParams p;
   p.Y = a.Y;
+  p.xscale = T::x_plane ? a.xscale : nullptr;
+  p.wscale = T::w_plane ? a.wscale : nullptr;
   p.N = a.N;
   p.K = a.K;
   p.M = a.M;
@@ -344,17 +978,65 @@ cudaError_t launch_cfg(const RunArgs& a) {
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_gemm_kernel<DT, BN, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  static unsigned attr_mask = 0;   // per device: dynamic shared memory opt-in done
+  const int dev = current_device();
+  if (!(attr_mask & (1u << (dev & 31)))) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_mask |= 1u << (dev & 31);
   }
   k<<<grid, kThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmB, p);
   return cudaGetLastError();
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+template <int DT, int BN, int STAGES>
+cudaError_t launch_widen(const RunArgs& a) {
+  using C = WCfg<DT, BN, STAGES>;
+  using WT = typename C::WT;
+  CUtensorMap tmA, tmR;
+  if (!make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K * 2,
+                C::K_PER_STAGE, kBM))
+    return cudaErrorInvalidValue;
+  bool ok;
+  if constexpr (WT::mx) {
+    ok = make_map_plain(&tmR, a.W, (uint64_t)a.K / 2, (uint64_t)a.M, (uint64_t)a.K / 2, 32, BN);
+  } else {
+    ok = make_map_plain(&tmR, a.W, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.M, BN, C::K_PER_STAGE);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  WParams p;
+  p.Y = a.Y;
+  p.wscale = a.wscale;
+  p.col_exp = nullptr;
+  p.N = a.N;
+  p.K = a.K;
+  p.M = a.M;
+  p.tiles_m = (a.N + kBM - 1) / kBM;
+  p.tiles_n = (a.M + BN - 1) / BN;
+  p.num_kb = (a.K + C::K_PER_STAGE - 1) / C::K_PER_STAGE;
+  p.dev_err = a.dev_err;
+  if constexpr (WT::mx) {
+    int8_t* ce = static_cast<int8_t*>(a.ws);
+    mx_row_exp_kernel<<<(a.M + 7) / 8, 256, 0, a.stream>>>(a.wscale, a.M, a.K / 32, ce);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    p.col_exp = ce;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = tiles < a.num_sms ? tiles : a.num_sms;
+  auto k = tc_widen_kernel<DT, BN, STAGES>;
+  static unsigned attr_mask = 0;
+  const int dev = current_device();
+  if (!(attr_mask & (1u << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_mask |= 1u << (dev & 31);
+  }
+  k<<<grid, kWThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmR, p);
+  return cudaGetLastError();
+}
+
+bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 }  // namespace
 
@@ -365,27 +1047,52 @@ bool tc_supported(int dt, int bn, int N, int K, int M) {
     case kFP16: return K % 8 == 0 && M % 8 == 0;
     case kI8I8:
     case kF8F8: return K % 16 == 0 && M % 16 == 0;
+    case kMX4X4: return bn == 128 && K % 32 == 0;
+    case kF4F4: return bn == 128 && K % 32 == 0 && M % 2 == 0;
+    case kMX8X4:
+    case kF8X4: return bn == 128 && K % 128 == 0;
+    case kINT8:
+    case kFP8: return K % 8 == 0 && M % 16 == 0;
+    case kMXFP4: return K % 32 == 0;
     default: return false;
   }
 }
 
 size_t tc_workspace(int dt, int bn, int N, int K, int M) {
-  (void)dt; (void)bn; (void)N; (void)K; (void)M;
+  (void)bn; (void)N;
+  if (dt == kF4F4) return (size_t)M * K / 2 + 256;   // the transposed weights
+  if (dt == kMXFP4) return (size_t)M + 256;          // per-row exponent offsets
   return 0;
 }
 
-int tc_launches(int dt) {
-  (void)dt;
-  return 1;
-}
+int tc_launches(int dt) { return (dt == kF4F4 || dt == kMXFP4) ? 2 : 1; }
 
 cudaError_t launch_tc(const RunArgs& a, int bn) {
   if (!tc_supported(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
-  if (!aligned16(a.X) || !aligned16(a.W) || !aligned16(a.Y)) return cudaErrorInvalidValue;
+  if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
   switch (a.dt) {
-    case kFP16: return bn == 256 ? launch_cfg<kFP16, 256, 4>(a) : launch_cfg<kFP16, 128, 6>(a);
-    case kI8I8: return bn == 256 ? launch_cfg<kI8I8, 256, 4>(a) : launch_cfg<kI8I8, 128, 6>(a);
-    case kF8F8: return bn == 256 ? launch_cfg<kF8F8, 256, 4>(a) : launch_cfg<kF8F8, 128, 6>(a);
+    case kFP16: return bn == 256 ? launch_cfg<kFP16, 256, 4>(a, a.W) : launch_cfg<kFP16, 128, 6>(a, a.W);
+    case kI8I8: return bn == 256 ? launch_cfg<kI8I8, 256, 4>(a, a.W) : launch_cfg<kI8I8, 128, 6>(a, a.W);
+    case kF8F8: return bn == 256 ? launch_cfg<kF8F8, 256, 4>(a, a.W) : launch_cfg<kF8F8, 128, 6>(a, a.W);
+    case kINT8: return bn == 256 ? launch_widen<kINT8, 256, 3>(a) : launch_widen<kINT8, 128, 5>(a);
+    case kFP8: return bn == 256 ? launch_widen<kFP8, 256, 3>(a) : launch_widen<kFP8, 128, 5>(a);
+    case kMXFP4: {
+      if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+      return bn == 256 ? launch_widen<kMXFP4, 256, 3>(a) : launch_widen<kMXFP4, 128, 5>(a);
+    }
+    case kMX4X4: return launch_cfg<kMX4X4, 128, 5>(a, a.W);
+    case kMX8X4: return launch_cfg<kMX8X4, 128, 5>(a, a.W);
+    case kF8X4: return launch_cfg<kF8X4, 128, 5>(a, a.W);
+    case kF4F4: {
+      if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M) || !aligned(a.ws, 256))
+        return cudaErrorInvalidValue;
+      dim3 grid((a.M + kTrM - 1) / kTrM, (a.K + kTrK - 1) / kTrK);
+      transpose_fp4_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W),
+                                                       static_cast<uint8_t*>(a.ws), a.K, a.M);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+      return launch_cfg<kF4F4, 128, 5>(a, a.ws);
+    }
     default: return cudaErrorInvalidValue;
   }
 }

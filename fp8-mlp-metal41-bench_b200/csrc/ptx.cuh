@@ -180,8 +180,8 @@ __device__ __forceinline__ void tc_mma_bs(uint32_t d_tmem, uint64_t adesc, uint6
   if constexpr (KIND == kKindMxF8F6F4) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.block32 [%0], %1, %2, %3, [%5], "
-        "[%6], p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], "
+        "p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
         : "memory");
   } else if constexpr (KIND == kKindMxF4) {

@@ -57,23 +57,44 @@ def assert_close(dtype, out, ref):
     return float(rel.max())
 
 
-TC_DTYPES = ["fp16", "i8i8", "f8f8"]
+# tensor-core tiles per dtype (block-scaled kinds run 128x128 only)
+TC_TILES = {d: ["128x256", "128x128"] for d in ("fp16", "i8i8", "f8f8", "int8", "fp8", "mxfp4")}
+TC_TILES.update({d: ["128x128"] for d in ("f4f4", "mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
+TC_CASES = [(d, t) for d in F.DTYPES for t in TC_TILES[d]]
 
 
-@pytest.mark.parametrize("dtype", TC_DTYPES)
-@pytest.mark.parametrize("tile", ["128x256", "128x128"])
-@pytest.mark.parametrize("shape", [(256, 512, 512), (200, 320, 272), (1000, 1024, 1296)])
+@pytest.mark.parametrize("dtype,tile", TC_CASES)
+@pytest.mark.parametrize("shape", [(256, 512, 512), (200, 384, 272), (1000, 1024, 1296)])
 def test_tensor_core_tiles(gemm, dtype, tile, shape):
     N, K, M = shape
     out, ref, _ = run_case(gemm, dtype, tile, N, K, M)
     assert_close(dtype, out, ref)
 
 
-@pytest.mark.parametrize("dtype", TC_DTYPES)
+@pytest.mark.parametrize("dtype", F.DTYPES)
 def test_tensor_core_reference_patterns(gemm, dtype):
     # the reference's own deterministic operands (main.swift:379-390)
-    out, ref, _ = run_case(gemm, dtype, "128x256", 384, 1024, 768, mode="ref")
+    tile = TC_TILES[dtype][0]
+    out, ref, _ = run_case(gemm, dtype, tile, 384, 1024, 768, mode="ref")
     assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("lo,hi", [(124, 130), (90, 100), (150, 160), (100, 145)])
+def test_mxfp4_widen_any_scale_range(gemm, lo, hi):
+    # E2M1 * 2^(s-127) leaves the f16 range outside s in [104, 140]; the
+    # per-row exponent offsets keep the widened weights exact
+    N, K, M = 256, 512, 384
+    ops = Operands(N, K, M, "seeded", 4)
+    rng = np.random.default_rng(9)
+    ops._cache["wscale"] = rng.integers(lo, hi + 1, M * (K // 32), dtype=np.uint8)
+    out, ref, _ = run_case(gemm, "mxfp4", "128x256", N, K, M, ops=ops)
+    if hi - lo <= 36:
+        assert_close("mxfp4", out, ref)
+    else:
+        # a row whose scales span more than f16's range loses only terms
+        # below 2^-24 of its largest block
+        rms = float(np.sqrt(np.mean(ref * ref)))
+        assert np.all(np.abs(out - ref) <= 1e-3 * np.maximum(np.abs(ref), 1e-2 * rms))
 
 
 @pytest.mark.parametrize("dtype", F.DTYPES)
