@@ -69,11 +69,13 @@ struct TileDef {
   const char* name;
   TileKind kind;
   int param;   // BN for tensor-core tiles, K splits for GEMV tiles
+  int bm;      // tensor-core tiles: 128 (one CTA) or 256 (a CTA pair)
 };
 const TileDef kTiles[] = {
-    {"128x256", kTileTC, 256},  {"128x128", kTileTC, 128},  {"gemv.k1", kTileGemv, 1},
-    {"gemv.k2", kTileGemv, 2},  {"gemv.k4", kTileGemv, 4},  {"gemv.k8", kTileGemv, 8},
-    {"gemv.k16", kTileGemv, 16}, {"gemv.k32", kTileGemv, 32}, {"gemv.k64", kTileGemv, 64},
+    {"256x256", kTileTC, 256, 256},  {"128x256", kTileTC, 256, 128}, {"128x128", kTileTC, 128, 128},
+    {"gemv.k1", kTileGemv, 1, 0},    {"gemv.k2", kTileGemv, 2, 0},   {"gemv.k4", kTileGemv, 4, 0},
+    {"gemv.k8", kTileGemv, 8, 0},    {"gemv.k16", kTileGemv, 16, 0}, {"gemv.k32", kTileGemv, 32, 0},
+    {"gemv.k64", kTileGemv, 64, 0},
 };
 constexpr int kNumTiles = (int)(sizeof(kTiles) / sizeof(kTiles[0]));
 
@@ -93,13 +95,13 @@ int layout_check(int dt, long N, long K, long M) {
 
 bool any_tc(int dt, int N, int K, int M) {
   for (int t = 0; t < kNumTiles; ++t)
-    if (kTiles[t].kind == kTileTC && tc_supported(dt, kTiles[t].param, N, K, M)) return true;
+    if (kTiles[t].kind == kTileTC && tc_supported(dt, kTiles[t].bm, kTiles[t].param, N, K, M)) return true;
   return false;
 }
 
 bool tile_ok(int dt, int t, int N, int K, int M) {
   if (!valid_tile(t) || layout_check(dt, N, K, M) != GEMM_OK) return false;
-  if (kTiles[t].kind == kTileTC) return tc_supported(dt, kTiles[t].param, N, K, M);
+  if (kTiles[t].kind == kTileTC) return tc_supported(dt, kTiles[t].bm, kTiles[t].param, N, K, M);
   // CUDA-core tiles: the thin-row kernel, and the fallback where no
   // tensor-core tile covers the dtype or shape.
   return N <= 16 || !any_tc(dt, N, K, M);
@@ -142,7 +144,7 @@ int enqueue(DevState* s, int dt, int tile, const void* X, const void* W, void* Y
   a.dev_err = s->dev_err;
   a.num_sms = s->num_sms;
   cudaError_t e;
-  if (kTiles[tile].kind == kTileTC) e = launch_tc(a, kTiles[tile].param);
+  if (kTiles[tile].kind == kTileTC) e = launch_tc(a, kTiles[tile].bm, kTiles[tile].param);
   else e = launch_gemv(a, kTiles[tile].param);
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return GEMM_OK;
@@ -246,8 +248,9 @@ int gemm_check_layout(int dtype, int N, int K, int M) {
 int gemm_default_tile(int dtype, int N, int K, int M) {
   if (layout_check(dtype, N, K, M) != GEMM_OK) return -1;
   if (N > 16) {
-    if (tc_supported(dtype, 256, N, K, M)) return gemm_tile_index("128x256");
-    if (tc_supported(dtype, 128, N, K, M)) return gemm_tile_index("128x128");
+    if (tc_supported(dtype, 256, 256, N, K, M)) return gemm_tile_index("256x256");
+    if (tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
+    if (tc_supported(dtype, 128, 128, N, K, M)) return gemm_tile_index("128x128");
   }
   int sms = 148;
   for (int d = 0; d < kMaxDevices; ++d)
@@ -418,8 +421,36 @@ int gemm_time_e2e(int device, int dtype, int tile, const void* hX, void* dX, con
 }
 
 int gemm_peak_probe(int device, int kind, int reps, int iters, double* tflops_out) {
-  (void)device; (void)kind; (void)reps; (void)iters; (void)tflops_out;
-  return fail(GEMM_ERR_ARGS, "peak probe not available in this build");
+  DevState* s = dev_state(device);
+  if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised", device);
+  if (kind < 0 || kind > 7 || reps < 1 || iters < 1 || !tflops_out) return fail(GEMM_ERR_ARGS, "bad probe arguments");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  const int ctas = kind >= 5 ? (s->num_sms / 2) * 2 : s->num_sms;
+  float* sink = nullptr;
+  if ((e = cudaMalloc(&sink, sizeof(float) * ctas)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  std::vector<cudaEvent_t> ev(2 * (size_t)iters);
+  for (auto& x : ev) cudaEventCreate(&x);
+  int rc = GEMM_OK;
+  // two untimed launches, then `iters` timed ones (tune/peak.swift:73-76)
+  for (int i = 0; i < 2 + iters && rc == GEMM_OK; ++i) {
+    if (i >= 2) cudaEventRecord(ev[2 * (i - 2)], s->stream);
+    e = launch_peak(kind, reps, ctas, sink, s->dev_err, s->stream);
+    if (e != cudaSuccess) rc = cuda_fail(e, "peak launch");
+    if (i >= 2) cudaEventRecord(ev[2 * (i - 2) + 1], s->stream);
+  }
+  if ((e = cudaStreamSynchronize(s->stream)) != cudaSuccess && rc == GEMM_OK) rc = cuda_fail(e, "peak sync");
+  if (rc == GEMM_OK) rc = check_dev_error(s, device);
+  if (rc == GEMM_OK) {
+    std::vector<float> ms(iters);
+    for (int i = 0; i < iters; ++i) cudaEventElapsedTime(&ms[i], ev[2 * i], ev[2 * i + 1]);
+    std::sort(ms.begin(), ms.end());
+    const double med = ms[iters / 2] * 1e-3;
+    *tflops_out = peak_flops_per_launch(kind, reps, ctas) / med / 1e12;
+  }
+  for (auto& x : ev) cudaEventDestroy(x);
+  cudaFree(sink);
+  return rc;
 }
 
 }  // extern "C"

@@ -9,9 +9,9 @@
 //   warp 1      TMEM allocator + single-thread MMA issuer: tcgen05.mma into a
 //               double-buffered TMEM accumulator, tcgen05.commit frees ring
 //               slots ("empty") and hands finished tiles to the epilogue
-//   warp 2      block-scaled kinds only: stages the UE8M0 scale factors of
-//               each ring slot in shared memory in the layout tcgen05.cp
-//               copies to TMEM (32 rows x 16 bytes per MMA and operand)
+//               for block-scaled kinds it also bulk-copies each stage's
+//               pre-packed UE8M0 blocks (sf_pack_kernel) and the MMA issuer
+//               moves them to TMEM with tcgen05.cp before each MMA
 //   warps 4-7   epilogue: tcgen05.ld TMEM -> registers -> Y, one TMEM lane
 //               quadrant (32 output rows) per warp
 //
@@ -107,8 +107,8 @@ struct Traits<kF8X4> {
 
 struct TcParams {
   void* Y;
-  const uint8_t* xscale;   // [N, K/32] UE8M0 or null (scale 1)
-  const uint8_t* wscale;   // [M, K/32] UE8M0 or null (scale 1)
+  const uint8_t* sfa;      // packed X scale blocks (see sf_pack_kernel) or null (scale 1)
+  const uint8_t* sfb;      // packed W scale blocks or null (scale 1)
   int N, K, M;
   int tiles_m, tiles_n, num_kb;
   int* dev_err;
@@ -127,7 +127,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // transaction bytes per stage: the 16U4_ALIGN16B load counts the packed
   // 4-bit source bytes (half of what it writes to shared memory)
-  static constexpr int STAGE_TX = A_BYTES + (T::b_unpack4 ? B_BYTES / 2 : B_BYTES);
+  static constexpr int STAGE_TX_AB = A_BYTES + (T::b_unpack4 ? B_BYTES / 2 : B_BYTES);
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;  // elements
   static constexpr int MMA_K_BYTES = 32;                     // K bytes per tcgen05.mma
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;  // 4
@@ -146,6 +146,7 @@ struct Cfg {
   static constexpr int SF_B_BYTES = SCALED ? MMAS_PER_STAGE * SF_B_CHUNKS * kSfChunk : 0;
   static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
   // TMEM: [0, 2*BN) accumulators; then per stage 4 columns per MMA for A and
   // 4*BN/128 per MMA for B (one 32-bit column per 32 rows, byte s = block s)
   static constexpr int ACC_COLS = BN;
@@ -153,7 +154,7 @@ struct Cfg {
   static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
   static constexpr int SF_COLS_STAGE = SCALED ? MMAS_PER_STAGE * (SF_COLS_A + SF_COLS_B) : 0;
   static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN + STAGES * SF_COLS_STAGE);
-  static constexpr int BAR_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;
+  static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
   static constexpr uint32_t IDESC =
       SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
@@ -181,32 +182,47 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int&
   tn = tile / tiles_m;
 }
 
-// Scale bytes of one row for the `nb` k-blocks starting at kblk0 (127 = 1.0
-// outside the matrix or without a plane).
-template <int NB>
-__device__ __forceinline__ void load_row_scales(const uint8_t* plane, int row, int rows, int kbpr,
-                                                int kblk0, uint8_t (&s)[NB]) {
-  if (plane == nullptr || row >= rows) {
+// Scale-factor packing pre-pass.  For every 128-row tile t of an operand,
+// every K stage st and every MMA kk of the stage, one 512-byte block:
+// byte (16*r0 + 4*j + s) = UE8M0 scale of row 128*t + r0 + 32*j for k-block
+// st*nb + kk*nsf + s (s < nsf; 127 = 1.0 outside the matrix).  That is the
+// source layout of tcgen05.cp.32x128b.warpx4: row r0's 16 bytes land in TMEM
+// lane r0 of every lane quadrant, 32-bit column j, where the block-scaled
+// MMA reads the scale of row r0 + 32*j.  The producer then fetches each
+// stage's blocks with one 1-D bulk copy per operand.
+struct SfPackJob {
+  const uint8_t* plane;   // [rows, kbpr]
+  uint8_t* out;           // [tiles][stages][4][512]
+  int rows, tiles;
+};
+
+__global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb, int kbpr, int stages, int nb,
+                                                      int nsf) {
+  const SfPackJob& j = blockIdx.y == 0 ? ja : jb;        // y = 0: X plane, 1: W plane
+  if (j.plane == nullptr) return;
+  const int tid = blockIdx.x * 256 + threadIdx.x;       // one thread per (t, st, kk, r0)
+  const int r0 = tid & 31;
+  const int kk = (tid >> 5) & 3;
+  const int rest = tid >> 7;
+  const int st = rest % stages, t = rest / stages;
+  if (t >= j.tiles) return;
+  const uint8_t* plane = j.plane;
+  const int rows = j.rows;
+  uint8_t* out = j.out;
+  uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < NB; ++i) s[i] = 127;
-    return;
-  }
-  const uint8_t* p = plane + (size_t)row * kbpr + kblk0;
-  const bool full = kblk0 + NB <= kbpr;
-  if (full && (reinterpret_cast<uintptr_t>(p) % NB) == 0) {
-    if constexpr (NB == 4) {
-      const uint32_t v = __ldg(reinterpret_cast<const uint32_t*>(p));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s[i] = (uint8_t)(v >> (8 * i));
-    } else {
-      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s[i] = (uint8_t)(v.x >> (8 * i)), s[4 + i] = (uint8_t)(v.y >> (8 * i));
+  for (int j = 0; j < 4; ++j) {
+    const int row = t * 128 + r0 + 32 * j;
+    uint32_t v = 0;
+    for (int q = 0; q < nsf; ++q) {
+      const int kblk = st * nb + kk * nsf + q;
+      const uint32_t sc = (row < rows && kblk < kbpr) ? plane[(size_t)row * kbpr + kblk] : 127u;
+      v |= sc << (8 * q);
     }
-  } else {
-#pragma unroll
-    for (int i = 0; i < NB; ++i) s[i] = (kblk0 + i < kbpr) ? __ldg(p + i) : (uint8_t)127;
+    w[j] = v;
   }
+  *reinterpret_cast<uint4*>(out + ((size_t)((t * stages + st) * 4 + kk)) * 512 + r0 * 16) =
+      make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int DT, int BN, int STAGES>
@@ -227,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->full[s], C::SCALED ? 2 : 1);   // producer (+ scale stager)
+      mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -243,6 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
+  if constexpr (C::SCALED) {
+    // a block of unit scales (127) for operands without a scale plane
+    if (warp == 2) {
+      *reinterpret_cast<uint4*>(smem + C::SF_CONST_OFF + lane * 16) =
+          make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+      fence_proxy_async_smem();
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -255,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool filled[8];
     for (int s = 0; s < STAGES; ++s) filled[s] = false, filled_parity[s] = 0;
     bool ok = true;
+    const uint32_t tx = C::STAGE_TX_AB + (p.sfa ? C::SF_A_BYTES : 0) + (p.sfb ? C::SF_B_BYTES : 0);
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, tm, tn);
@@ -262,7 +287,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x100 + stage)) { ok = false; break; }
         unsigned char* a_dst = smem + stage * C::STAGE_BYTES;
         unsigned char* b_dst = a_dst + C::A_BYTES;
-        mbar_arrive_expect_tx(&bars->full[stage], C::STAGE_TX);
+        mbar_arrive_expect_tx(&bars->full[stage], tx);
+        if constexpr (C::SCALED) {
+          unsigned char* sf = smem + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+          if (p.sfa)
+            bulk_load(sf, p.sfa + (size_t)(tm * p.num_kb + kb) * C::SF_A_BYTES, C::SF_A_BYTES, &bars->full[stage]);
+          if (p.sfb) {
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              bulk_load(sf + C::SF_A_BYTES + c * C::SF_A_BYTES,
+                        p.sfb + (size_t)((tn * C::SF_B_CHUNKS + c) * p.num_kb + kb) * C::SF_A_BYTES,
+                        C::SF_A_BYTES, &bars->full[stage]);
+          }
+        }
         // A tile: x in elements of the map (bytes for 8/4-bit maps)
         tma_load_2d(a_dst, &tmA, &bars->full[stage], kb * (T::a_bits == 16 ? C::K_PER_STAGE : kRowBytes),
                     tm * kBM);
@@ -309,16 +346,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t b_addr = a_addr + C::A_BYTES;
         if constexpr (C::SCALED) {
           const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+          const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
           const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
           for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
             const uint32_t sfa_t = sf_tmem + kk * (C::SF_COLS_A + C::SF_COLS_B);
             const uint32_t sfb_t = sfa_t + C::SF_COLS_A;
-            tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(sf_smem + kk * kSfChunk, 0, 128));
+            tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + kk * kSfChunk : sf_const, 0, 128));
 #pragma unroll
             for (int c = 0; c < C::SF_B_CHUNKS; ++c)
               tc_cp_32x128b_warpx4(sfb_t + 4 * c,
-                                   sdesc_plain(sf_smem + C::SF_A_BYTES + (kk * C::SF_B_CHUNKS + c) * kSfChunk, 0, 128));
+                                   sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::MMAS_PER_STAGE + kk) * kSfChunk
+                                                     : sf_const, 0, 128));
             const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
             const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
             tc_mma_bs<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u, sfa_t, sfb_t);
@@ -336,68 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       tc_commit(&bars->acc_full[buf]);
-    }
-  } else if (warp == 2 && C::SCALED) {
-    // ------------------------ scale-factor stager ------------------------------
-    // For MMA kk of a stage, row r = r0 + 32*j of the operand tile: byte
-    // (16*r0 + 4*j + s) of its 512-byte block holds the scale of k-block
-    // kk*nsf + s; tcgen05.cp 32x128b.warpx4 puts row r0's 16 bytes into TMEM
-    // lane r0 (replicated to all four lane quadrants), 32-bit column j.
-    constexpr int NB = C::KBLK_PER_STAGE;   // 4 (mxf8f6f4) or 8 (mxf4)
-    const int kbpr = p.K / 32;
-    uint32_t stage = 0, phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int tm, tn;
-      tile_coords(tile, p.tiles_m, tm, tn);
-      bool ok = true;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        const bool got = mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x500 + stage);
-        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-        unsigned char* sf = smem + C::SF_OFF + stage * C::SF_STAGE_BYTES;
-        const int kblk0 = kb * NB;
-        // A (X rows of this tile)
-        {
-          uint8_t s[4][NB];
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            load_row_scales<NB>(T::x_plane ? p.xscale : nullptr, tm * kBM + lane + 32 * j, p.N, kbpr, kblk0, s[j]);
-#pragma unroll
-          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              w[j] = s[j][kk * T::nsf];
-              if constexpr (T::nsf == 2) w[j] |= (uint32_t)s[j][kk * T::nsf + 1] << 8;
-            }
-            *reinterpret_cast<uint4*>(sf + kk * kSfChunk + lane * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        // B (W rows = output columns of this tile)
-#pragma unroll
-        for (int c = 0; c < C::SF_B_CHUNKS; ++c) {
-          uint8_t s[4][NB];
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            load_row_scales<NB>(T::w_plane ? p.wscale : nullptr, tn * BN + c * 128 + lane + 32 * j, p.M, kbpr,
-                                kblk0, s[j]);
-#pragma unroll
-          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              w[j] = s[j][kk * T::nsf];
-              if constexpr (T::nsf == 2) w[j] |= (uint32_t)s[j][kk * T::nsf + 1] << 8;
-            }
-            *reinterpret_cast<uint4*>(sf + C::SF_A_BYTES + (kk * C::SF_B_CHUNKS + c) * kSfChunk + lane * 16) =
-                make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        fence_proxy_async_smem();   // generic-proxy writes -> visible to tcgen05.cp
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars->full[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
-      }
-      if (!ok) break;
     }
   } else if (warp >= 4) {
     // ------------------------------ epilogue ----------------------------------
@@ -504,6 +481,201 @@ __global__ void __launch_bounds__(256) transpose_fp4_kernel(const uint8_t* __res
       const uint8_t* b = reinterpret_cast<const uint8_t*>(o);
       for (int j = 0; j < (K - k0 - kk0) / 2; ++j) dst[j] = b[j];
     }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// 2-CTA variant (cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256 x BN tile.  Each CTA loads its own 128 rows of X and its own BN/2
+// columns of W (halving the operand stream per SM against the 1-CTA 128 x BN
+// tile), the pair's leader issues tcgen05.mma.cta_group::2 (M = 256) over
+// both CTAs' shared memory, and each CTA's TMEM holds its 128 rows of the
+// accumulator.  Completion of both CTAs' TMA loads is counted on the
+// leader's "full" barrier; the leader's tcgen05.commit multicasts to the
+// "empty" / "acc_full" barriers of both CTAs; both epilogues release the
+// accumulator on the leader's "acc_empty".  No TMA load uses multicast.
+// ----------------------------------------------------------------------------
+template <int DT, int BN, int STAGES>
+struct Cfg2 {
+  using T = Traits<DT>;
+  static constexpr int BH = BN / 2;                          // W columns per CTA
+  static constexpr int A_BYTES = kBM * kRowBytes;
+  static constexpr int B_BYTES = BH * kRowBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;
+  static constexpr int MMA_K_BYTES = 32;
+  static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;
+  static constexpr int B_BOX_MN = kRowBytes * 8 / T::b_bits;
+  static constexpr int B_BOXES = T::b_mn ? BH / B_BOX_MN : 1;
+  static constexpr int B_BOX_BYTES = T::b_mn ? K_PER_STAGE * kRowBytes : B_BYTES;
+  static constexpr uint32_t B_LBO = T::b_mn ? (uint32_t)B_BOX_BYTES : 16u;
+  static constexpr uint32_t B_ADV = T::b_mn ? (uint32_t)(MMA_K_BYTES * 8 / T::b_bits) * kRowBytes
+                                            : (uint32_t)MMA_K_BYTES;
+  static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN);
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr uint32_t IDESC =
+      (T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | ((T::b_mn ? 1u : 0u) << 16) |
+      ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+  static_assert(T::nsf == 0, "block-scaled kinds use the 1-CTA kernel");
+  static_assert(!T::b_mn || BH % B_BOX_MN == 0, "W half-tile must be whole swizzle atoms");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <int DT, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        TcParams p) {
+  using C = Cfg2<DT, BN, STAGES>;
+  using T = typename C::T;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + C::BAR_OFF);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();             // 0 = leader
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_tiles = p.tiles_m * p.tiles_n;          // tiles of 256 x BN
+  AbortCtl ctl{p.dev_err, &bars->abort_flag};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);                     // the leader arms it for both CTAs
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 2 * 4);            // one arrival per epilogue warp, both CTAs
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem_base, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+  bool aborted_any = false;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------ TMA producer (both CTAs) ------------------------
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x100 + stage)) { ok = false; break; }
+        const uint32_t lfull = mapa_shared(&bars->full[stage], 0);
+        unsigned char* a_dst = smem + stage * C::STAGE_BYTES;
+        unsigned char* b_dst = a_dst + C::A_BYTES;
+        // Only the leader arrives, expecting both CTAs' bytes; the peer's loads
+        // just complete their transactions on the leader's barrier (a remote
+        // arrive per stage would put a cross-SM round trip in the peer's loop).
+        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * C::STAGE_BYTES);
+        tma_load_2d_pair(a_dst, &tmA, lfull, kb * (T::a_bits == 16 ? C::K_PER_STAGE : kRowBytes),
+                         tm * 256 + (int)rank * kBM);
+        if constexpr (T::b_mn) {
+#pragma unroll
+          for (int j = 0; j < C::B_BOXES; ++j)
+            tma_load_2d_pair(b_dst + j * C::B_BOX_BYTES, &tmB, lfull, tn * BN + (int)rank * C::BH + j * C::B_BOX_MN,
+                             kb * C::K_PER_STAGE);
+        } else {
+          tma_load_2d_pair(b_dst, &tmB, lfull, kb * kRowBytes, tn * BN + (int)rank * C::BH);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+    aborted_any = !ok;
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------ MMA issuer (leader only) ------------------------
+    uint32_t stage = 0, phase = 0;
+    int local = 0;
+    bool ok = true;
+    const uint32_t smem_base = smem_u32(smem);
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      if (!mbar_wait(&bars->acc_empty[buf], acc_par ^ 1u, ctl, 0x200 + buf)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x300 + stage)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
+        const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+          const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
+          const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+          tc_mma_pair<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+        }
+        tc_commit_pair(&bars->empty[stage], 0x3);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok) break;
+      tc_commit_pair(&bars->acc_full[buf], 0x3);
+    }
+    aborted_any = !ok;
+  } else if (warp >= 4) {
+    // ------------------------ epilogue (both CTAs) ----------------------------
+    const int q = warp - 4;
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
+      int tm, tn;
+      tile_coords(tile, p.tiles_m, tm, tn);
+      const int buf = local & 1;
+      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const bool got = mbar_wait(&bars->acc_full[buf], acc_par, ctl, 0x400 + buf);
+      if (!__all_sync(0xffffffffu, got)) { aborted_any = true; break; }
+      __syncwarp();
+      tc_fence_after();
+      const int row = tm * 256 + (int)rank * kBM + q * 32 + lane;
+      const int col0 = tn * BN;
+      const bool row_ok = row < p.N;
+      uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
+      const bool vec_ok = (p.M % 4) == 0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + c * 32), r);
+        tmem_ld_wait();
+        const int cb = col0 + c * 32;
+        if (row_ok) {
+          if (vec_ok && cb + 32 <= p.M) {
+            uint4* dst = reinterpret_cast<uint4*>(yrow + cb);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (cb + v < p.M) yrow[cb + v] = r[v];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
+    }
+  }
+
+  if (aborted_any || aborted(ctl)) {
+    // let TMA copies still in flight (ours or the peer's) land before exiting
+    const unsigned long long t0 = global_ns();
+    while (global_ns() - t0 < 100000ull) {}
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -936,7 +1108,8 @@ int current_device() {
 }
 
 template <int DT, int BN, int STAGES>
-cudaError_t launch_cfg(const RunArgs& a, const void* W) {
+cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nullptr,
+                       const uint8_t* sfb = nullptr) {
   using C = Cfg<DT, BN, STAGES>;
   using T = typename C::T;
   CUtensorMap tmA, tmB;
@@ -966,8 +1139,8 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W) {
 
   TcParams p;
   p.Y = a.Y;
-  p.xscale = T::x_plane ? a.xscale : nullptr;
-  p.wscale = T::w_plane ? a.wscale : nullptr;
+  p.sfa = sfa;
+  p.sfb = sfb;
   p.N = a.N;
   p.K = a.K;
   p.M = a.M;
@@ -987,6 +1160,72 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W) {
   }
   k<<<grid, kThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmB, p);
   return cudaGetLastError();
+}
+
+template <int DT, int BN, int STAGES>
+cudaError_t launch_pair(const RunArgs& a) {
+  using C = Cfg2<DT, BN, STAGES>;
+  using T = typename C::T;
+  CUtensorMap tmA, tmB;
+  const CUtensorMapDataType ty8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  bool ok;
+  if constexpr (T::a_bits == 16) {
+    ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K * 2,
+                  C::K_PER_STAGE, kBM);
+  } else {
+    const uint64_t row_bytes = (uint64_t)a.K * T::a_bits / 8;
+    ok = make_map(&tmA, a.X, ty8, row_bytes, (uint64_t)a.N, row_bytes, kRowBytes, kBM);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  if constexpr (T::b_mn) {
+    const int es = T::b_bits / 8;
+    ok = make_map(&tmB, a.W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, (uint64_t)a.M, (uint64_t)a.K,
+                  (uint64_t)a.M * es, C::B_BOX_MN, C::K_PER_STAGE);
+  } else {
+    const uint64_t row_bytes = (uint64_t)a.K * T::b_bits / 8;
+    ok = make_map(&tmB, a.W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  TcParams p;
+  p.Y = a.Y;
+  p.sfa = nullptr;
+  p.sfb = nullptr;
+  p.N = a.N;
+  p.K = a.K;
+  p.M = a.M;
+  p.tiles_m = (a.N + 255) / 256;
+  p.tiles_n = (a.M + BN - 1) / BN;
+  p.num_kb = (a.K + C::K_PER_STAGE - 1) / C::K_PER_STAGE;
+  p.dev_err = a.dev_err;
+  const int tiles = p.tiles_m * p.tiles_n;
+  auto k = tc_gemm_pair_kernel<DT, BN, STAGES>;
+  static unsigned attr_mask = 0;
+  static int max_pairs[32] = {0};   // co-resident CTA pairs per device (persistent grid size)
+  const int dev = current_device();
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!(attr_mask & (1u << (dev & 31)))) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    cfg.gridDim = dim3(a.num_sms);
+    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) n = a.num_sms / 2;
+    max_pairs[dev & 31] = n;
+    attr_mask |= 1u << (dev & 31);
+  }
+  const int cap = max_pairs[dev & 31] > 0 ? max_pairs[dev & 31] : a.num_sms / 2;
+  const int pairs = tiles < cap ? tiles : cap;
+  cfg.gridDim = dim3(2 * pairs);
+  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, p);
 }
 
 template <int DT, int BN, int STAGES>
@@ -1040,9 +1279,16 @@ bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p)
 
 }  // namespace
 
-bool tc_supported(int dt, int bn, int N, int K, int M) {
+bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
   if (bn != 128 && bn != 256) return false;
   if (N <= 0 || K <= 0 || M <= 0) return false;
+  if (bm == 256) {   // CTA-pair tiles: the unscaled kinds, 256-wide
+    if (bn != 256) return false;
+    if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
+    if (dt == kI8I8 || dt == kF8F8) return K % 16 == 0 && M % 16 == 0;
+    return false;
+  }
+  if (bm != 128) return false;
   switch (dt) {
     case kFP16: return K % 8 == 0 && M % 8 == 0;
     case kI8I8:
@@ -1058,18 +1304,87 @@ bool tc_supported(int dt, int bn, int N, int K, int M) {
   }
 }
 
+namespace {
+
+size_t round256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace of the block-scaled kinds: [packed X scales][packed W scales]
+// [f4f4: W transposed to [M,K]].
+struct ScaledWs {
+  size_t a_bytes = 0, b_bytes = 0, wt_bytes = 0;
+  int stages = 0, a_tiles = 0, b_tiles = 0, nb = 0, nsf = 0;
+  size_t total() const { return round256(a_bytes) + round256(b_bytes) + round256(wt_bytes); }
+};
+
+ScaledWs scaled_ws(int dt, int bn, int N, int K, int M) {
+  ScaledWs w;
+  const bool mxf4 = (dt == kMX4X4 || dt == kF4F4);
+  const int kps = mxf4 ? 256 : 128;
+  w.nb = kps / 32;
+  w.nsf = mxf4 ? 2 : 1;
+  w.stages = (K + kps - 1) / kps;
+  w.a_tiles = (N + 127) / 128;
+  w.b_tiles = (M + bn - 1) / bn * (bn / 128);
+  const bool xp = (dt == kMX4X4 || dt == kMX8X4), wp = (dt != kF4F4);
+  if (xp) w.a_bytes = (size_t)w.a_tiles * w.stages * 4 * kSfChunk;
+  if (wp) w.b_bytes = (size_t)w.b_tiles * w.stages * 4 * kSfChunk;
+  if (dt == kF4F4) w.wt_bytes = (size_t)M * K / 2;
+  return w;
+}
+
+bool is_scaled(int dt) { return dt == kMX4X4 || dt == kMX8X4 || dt == kF8X4 || dt == kF4F4; }
+
+template <int DT, int BN, int STAGES>
+cudaError_t launch_scaled(const RunArgs& a) {
+  const ScaledWs w = scaled_ws(DT, BN, a.N, a.K, a.M);
+  if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
+  uint8_t* base = static_cast<uint8_t*>(a.ws);
+  uint8_t* pa = w.a_bytes ? base : nullptr;
+  uint8_t* pb = w.b_bytes ? base + round256(w.a_bytes) : nullptr;
+  uint8_t* wt = base + round256(w.a_bytes) + round256(w.b_bytes);
+  cudaError_t e;
+  if (pa || pb) {
+    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles};
+    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles};
+    const int tiles = w.a_tiles > w.b_tiles ? w.a_tiles : w.b_tiles;
+    const int threads = tiles * w.stages * 128;
+    sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.nsf);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  const void* W = a.W;
+  if constexpr (DT == kF4F4) {
+    dim3 grid((a.M + kTrM - 1) / kTrM, (a.K + kTrK - 1) / kTrK);
+    transpose_fp4_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), wt, a.K, a.M);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    W = wt;
+  }
+  return launch_cfg<DT, BN, STAGES>(a, W, pa, pb);
+}
+
+}  // namespace
+
 size_t tc_workspace(int dt, int bn, int N, int K, int M) {
-  (void)bn; (void)N;
-  if (dt == kF4F4) return (size_t)M * K / 2 + 256;   // the transposed weights
+  if (is_scaled(dt)) return scaled_ws(dt, bn, N, K, M).total();
   if (dt == kMXFP4) return (size_t)M + 256;          // per-row exponent offsets
   return 0;
 }
 
-int tc_launches(int dt) { return (dt == kF4F4 || dt == kMXFP4) ? 2 : 1; }
+int tc_launches(int dt) {
+  if (dt == kMXFP4 || dt == kF4F4 || dt == kMX4X4 || dt == kMX8X4 || dt == kF8X4) return 2;
+  return 1;
+}
 
-cudaError_t launch_tc(const RunArgs& a, int bn) {
-  if (!tc_supported(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
+  if (!tc_supported(a.dt, bm, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
   if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
+  if (bm == 256) {
+    switch (a.dt) {
+      case kFP16: return launch_pair<kFP16, 256, 6>(a);
+      case kI8I8: return launch_pair<kI8I8, 256, 6>(a);
+      case kF8F8: return launch_pair<kF8F8, 256, 6>(a);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.dt) {
     case kFP16: return bn == 256 ? launch_cfg<kFP16, 256, 4>(a, a.W) : launch_cfg<kFP16, 128, 6>(a, a.W);
     case kI8I8: return bn == 256 ? launch_cfg<kI8I8, 256, 4>(a, a.W) : launch_cfg<kI8I8, 128, 6>(a, a.W);
@@ -1080,19 +1395,10 @@ cudaError_t launch_tc(const RunArgs& a, int bn) {
       if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
       return bn == 256 ? launch_widen<kMXFP4, 256, 3>(a) : launch_widen<kMXFP4, 128, 5>(a);
     }
-    case kMX4X4: return launch_cfg<kMX4X4, 128, 5>(a, a.W);
-    case kMX8X4: return launch_cfg<kMX8X4, 128, 5>(a, a.W);
-    case kF8X4: return launch_cfg<kF8X4, 128, 5>(a, a.W);
-    case kF4F4: {
-      if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M) || !aligned(a.ws, 256))
-        return cudaErrorInvalidValue;
-      dim3 grid((a.M + kTrM - 1) / kTrM, (a.K + kTrK - 1) / kTrK);
-      transpose_fp4_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W),
-                                                       static_cast<uint8_t*>(a.ws), a.K, a.M);
-      cudaError_t e = cudaGetLastError();
-      if (e != cudaSuccess) return e;
-      return launch_cfg<kF4F4, 128, 5>(a, a.ws);
-    }
+    case kMX4X4: return launch_scaled<kMX4X4, 128, 5>(a);
+    case kMX8X4: return launch_scaled<kMX8X4, 128, 5>(a);
+    case kF8X4: return launch_scaled<kF8X4, 128, 5>(a);
+    case kF4F4: return launch_scaled<kF4F4, 128, 5>(a);
     default: return cudaErrorInvalidValue;
   }
 }

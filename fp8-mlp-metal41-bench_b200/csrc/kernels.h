@@ -28,11 +28,11 @@ size_t gemv_workspace(int dt, int ksplit, int N, int K, int M);
 cudaError_t launch_gemv(const RunArgs& a, int ksplit);
 
 // ---- tcgen05 tensor-core GEMM --------------------------------------------------
-// bn: output tile width (128 or 256); bm is 128.
-bool tc_supported(int dt, int bn, int N, int K, int M);
+// bm: 128 (one CTA per tile) or 256 (a CTA pair, cta_group::2); bn: 128 or 256.
+bool tc_supported(int dt, int bm, int bn, int N, int K, int M);
 size_t tc_workspace(int dt, int bn, int N, int K, int M);
 int tc_launches(int dt);
-cudaError_t launch_tc(const RunArgs& a, int bn);
+cudaError_t launch_tc(const RunArgs& a, int bm, int bn);
 
 // Record a message for gemm_last_error() (defined in api.cu).
 void set_last_error(const char* msg);

@@ -183,10 +183,13 @@ int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const voi
                      int N, int K, int M, const void *xscale, const void *wscale, void *stream);
 
 /* ---- pure-compute peak probe (tune/peak.metal + tune/peak.swift) ------------ */
-/* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4.
- * Runs `iters` launches of a kernel that issues `reps` tcgen05.mma per CTA
- * on operands resident in shared memory (no global traffic in the loop) and
- * reports the median dense TFLOP/s (TOP/s for i8). */
+/* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4, and
+ * 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2).  Runs 2 untimed and
+ * `iters` timed launches of a kernel that issues reps x 4 tcgen05.mma
+ * (128 x 256 per CTA, or 256 x 256 per pair) on operands resident in shared
+ * memory, no global traffic in the loop (tune/peak.metal:29-87), and
+ * reports the median dense TFLOP/s (TOP/s for i8).  The probe allocates a
+ * few hundred bytes of device memory for its result sink. */
 int gemm_peak_probe(int device, int kind, int reps, int iters, double *tflops_out);
 
 #ifdef __cplusplus

@@ -43,7 +43,7 @@ def test_dtype_and_kernel_names_match_reference():
 
 def test_tile_table():
     names = G.tile_names()
-    assert "128x256" in names and "128x128" in names
+    assert "256x256" in names and "128x256" in names and "128x128" in names
     assert all(G.tile_index(n) == i for i, n in enumerate(names))
     assert G.tile_index("64x32") == -1
 
@@ -57,7 +57,7 @@ def test_layout_rules_and_tile_support():
     assert not G.tile_supported(F.CODE["i8i8"], t256, 4096, 4100, 4096)   # TMA stride rule
     # thin rows: the CUDA-core kernel; the default tile is a gemv tile
     assert G.tile_names()[G.default_tile(F.CODE["int8"], 1, 4096, 11008)].startswith("gemv")
-    assert G.tile_names()[G.default_tile(F.CODE["i8i8"], 4096, 4096, 4096)] == "128x256"
+    assert G.tile_names()[G.default_tile(F.CODE["i8i8"], 4096, 4096, 4096)] == "256x256"
 
 
 def test_workspace_sizes():
