@@ -259,6 +259,7 @@ def traffic_for(kernel_key):
 
 
 def ours(a):
+    from mlpgemm import dist_util as DU
     from mlpgemm import formats as F
     from mlpgemm import lib as G
     from mlpgemm.data import Operands
@@ -308,15 +309,10 @@ def ours(a):
     barrier()
     total_ms = float(sum(ms))
     if dist is not None:
-        import torch
-        t = torch.tensor([total_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-        okt = torch.tensor([1 if ok else 0], device="cuda")
-        dist.all_reduce(okt, op=dist.ReduceOp.MIN)
-        ok = bool(okt.item())
+        total_ms = DU.reduce_max(dist, total_ms, "cuda")
+        ok = DU.reduce_all(dist, ok, "cuda")
     flops = 2.0 * N * K * M
-    value = flops * world * a.steps / (total_ms / 1e3) / 1e12
+    value = DU.weak_scaling_rate(flops, world, a.steps, total_ms)
 
     # end to end through the C ABI: pinned host X in, device GEMM, host Y out
     e2e = None

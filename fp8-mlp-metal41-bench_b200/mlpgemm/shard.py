@@ -1,0 +1,246 @@
+"""M-sharded GEMM across the GPUs of one node (strong scaling).
+
+Run under torchrun, one process per GPU:
+
+    torchrun --nproc-per-node G --master-addr 127.0.0.1 mlp_bench.py --gpus G ...
+
+The reference is single-device (main.swift:272); this is the build's own
+multi-GPU mode.  The GEMM Y[N,M] = X[N,K] @ W[K,M] partitions along M with
+no exchange inside it:
+
+  * X is generated on rank 0 and broadcast once over NCCL (timed separately,
+    `bcast_ms`), so every GPU holds the same activations;
+  * W is column-sliced: GPU g owns the contiguous block [m0_g, m0_g + w_g)
+    (the [M,K] mxfp4 weights and their scale planes are row slices); every
+    rank derives its slice from the same seeded generator, so no weight
+    bytes move;
+  * each GPU runs libgemm.so on its block, timed with CUDA events on its
+    own device; the aggregate rate is 2*N*K*M / max over GPUs of the
+    per-GPU median time;
+  * --allgather gathers the Y blocks over NCCL (NVLink) into [G, N, w] and
+    lays them out as [N, M] on every GPU; that collective is timed
+    separately (`allgather_ms`) and does not enter the GEMM rate.
+
+torch.distributed is plumbing here (device buffers, NCCL, barriers); the
+GEMM itself is libgemm.so through its C ABI.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import statistics
+import sys
+
+import numpy as np
+
+from . import formats as F
+from . import lib as G
+from .data import Operands, shard_columns
+from .driver import (BenchExit, Row, check_samples, choose_tile, render_table, sample_points,
+                     table_line, tile_dims)
+
+
+def _init_dist():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    use_cuda = torch.cuda.is_available()
+    if use_cuda:
+        torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        dist.init_process_group("nccl" if use_cuda else "gloo",
+                                timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if use_cuda else None)
+    return torch, dist, world, rank, local, use_cuda
+
+
+def shard_plan(M: int, world: int):
+    """(m0, width) of every rank: widths rounded up to 32 columns so that
+    every block keeps the TMA stride and FP4 byte alignment."""
+    base = -(-M // world)
+    base = -(-base // 32) * 32 if world > 1 else base
+    out = []
+    for g in range(world):
+        m0 = min(g * base, M)
+        out.append((m0, min(m0 + base, M) - m0))
+    return out
+
+
+def _x_bytes_tensor(torch, ops: Operands, dtype: str, device):
+    x = ops.X(dtype)
+    return torch.from_numpy(x.view(np.uint8).copy()).to(device)
+
+
+def run_shape(a, shape, torch, dist, world, rank, local, profile):
+    N, K, M = shape.N, shape.K, shape.M
+    flops = 2.0 * N * K * M
+    rows = []
+    extra = []
+    plan = shard_plan(M, world)
+    m0, width = plan[rank]
+    dev = torch.device("cuda", local)
+    medians = {}
+    for dtype in a.dtypes:
+        if not F.layout_ok(dtype, N, K, M):
+            raise BenchExit(1, f"{dtype} needs even X/W counts and K a multiple of 32 "
+                               f"(128 for FP8 × MXFP4)")
+        ops = Operands(N, K, M, a.data, a.seed)
+        dt = F.CODE[dtype]
+        tile = choose_tile(a, profile, dtype, N, K, width) if width > 0 else "gemv.k1"
+        ti = G.tile_index(tile)
+        # X: rank 0 generates and broadcasts once (NCCL), timed separately
+        nbx = F.x_bytes(dtype, N, K)
+        X = torch.empty(nbx, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            X.copy_(_x_bytes_tensor(torch, ops, dtype, dev))
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        dist.broadcast(X, src=0)
+        ev1.record()
+        torch.cuda.synchronize()
+        bcast_ms = ev0.elapsed_time(ev1)
+        xs = ops.xscale(dtype)
+        XS = None
+        if xs is not None:
+            XS = torch.from_numpy(xs.copy()).to(dev)
+            dist.broadcast(XS, src=0)
+        # this rank's weight block
+        Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
+        assert w == width
+        Wt = torch.from_numpy(Wsh.copy()).to(dev)
+        WS = torch.from_numpy(wsc.copy()).to(dev) if wsc is not None else None
+        Y = torch.zeros(N * max(width, 1), dtype=torch.int32 if dtype == "i8i8" else torch.float32, device=dev)
+        wsb = G.workspace_size(dt, ti, N, K, width) if width > 0 else 0
+        WSP = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev) if wsb else None
+        torch.cuda.synchronize()
+        if width > 0:
+            ms = G.time(local, dt, ti, X, [Wt], Y, N, K, width, xscale=XS, wscales=[WS] if WS is not None else None,
+                        workspace=WSP, workspace_bytes=wsb, warmup=a.warmup, iters=shape.iters)
+            med = sorted(ms)[len(ms) // 2]
+        else:
+            med = 0.0
+        t = torch.tensor([med], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        med_max = float(t.item()) / 1000.0
+        medians[dtype] = med_max
+        # result check on this rank's block (sample points of its block)
+        rel = 0.0
+        if width > 0:
+            host = Y.cpu().numpy().reshape(N, width)
+            bm, bn = tile_dims(tile)
+            sub = _SubOps(ops, m0, width)
+            rel = check_samples(sub, dtype, host, sample_points(N, width, bm, bn), shape.name)
+        r = torch.tensor([rel], dtype=torch.float64, device=dev)
+        dist.all_reduce(r, op=dist.ReduceOp.MAX)
+        rel = float(r.item())
+        # optional all-gather of Y over NCCL, timed separately
+        ag_ms = None
+        if a.allgather:
+            wmax = max(wd for _, wd in plan)
+            Ypad = torch.zeros(N * wmax, dtype=Y.dtype, device=dev)
+            if width > 0:
+                Ypad.view(N, wmax)[:, :width].copy_(Y.view(N, width))
+            out = torch.empty(world * N * wmax, dtype=Y.dtype, device=dev)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            dist.all_gather_into_tensor(out, Ypad)
+            full = torch.empty(N, M, dtype=Y.dtype, device=dev)
+            blocks = out.view(world, N, wmax)
+            for g, (g0, gw) in enumerate(plan):
+                if gw:
+                    full[:, g0:g0 + gw].copy_(blocks[g, :, :gw])
+            e1.record()
+            torch.cuda.synchronize()
+            ag_ms = e0.elapsed_time(e1)
+            t = torch.tensor([ag_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ag_ms = float(t.item())
+            if rank == 0:   # the gathered matrix equals the blocks (spot check)
+                for g, (g0, gw) in enumerate(plan):
+                    if gw:
+                        assert torch.equal(full[:, g0:g0 + gw], blocks[g, :, :gw])
+        if dtype == "fp16":
+            vs = "1.000"
+        elif "fp16" in medians:
+            vs = "%.3f" % (medians["fp16"] / med_max)
+        else:
+            vs = "-"
+        rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
+                        rel, gpus=world, allgather_ms=ag_ms))
+        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, width))
+    return rows, extra
+
+
+class _SubOps:
+    """Operands view of one column block (for the sample-point check)."""
+
+    def __init__(self, ops: Operands, m0: int, width: int):
+        self.ops, self.m0, self.width = ops, m0, width
+
+    def x_rows(self, dtype, rows):
+        return self.ops.x_rows(dtype, rows)
+
+    def w_cols(self, dtype, cols):
+        return self.ops.w_cols(dtype, [c + self.m0 for c in cols])
+
+
+def main_sharded(a, shapes) -> int:
+    torch, dist, world, rank, local, use_cuda = _init_dist()
+    if not use_cuda:
+        raise BenchExit(1, "No CUDA device")
+    if a.gpus != world:
+        raise BenchExit(1, f"--gpus {a.gpus} but WORLD_SIZE={world}: launch one process per GPU with torchrun")
+    G.init(local)
+    name, arch, _ = G.device_info(local)
+    if rank == 0:
+        print(f"device: {name} x{world}")
+        print("timing: gpu")
+        print(f"dtypes: {','.join(a.dtypes)}")
+        print("shapes: " + " | ".join(f"{s.name} N={s.N} K={s.K} M={s.M} iters={s.iters}" for s in shapes))
+        print(f"loaded: {G.LIB_PATH}")
+        print(f"architecture: {arch}")
+        print(f"tiles: {'--tile ' + a.tile if a.tile else 'built-in defaults per shard'}")
+        print(f"data: {a.data} seed={a.seed}  sharding: M across {world} GPUs"
+              + (", Y all-gathered over NCCL" if a.allgather else ""))
+        sys.stdout.flush()
+    rows, extra = [], []
+    # warm the communicator up so the timed broadcast / all-gather exclude NCCL setup
+    w = torch.zeros(1 << 20, dtype=torch.uint8, device=torch.device("cuda", local))
+    dist.broadcast(w, src=0)
+    dist.all_gather_into_tensor(torch.empty(world << 20, dtype=torch.uint8, device=w.device), w)
+    torch.cuda.synchronize()
+    try:
+        for s in shapes:
+            r, e = run_shape(a, s, torch, dist, world, rank, local, {})
+            rows += r
+            extra += e
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print("")
+        for line in render_table(rows):
+            print(line)
+        print("")
+        hdr = " ".join([_c("shape", 8), _c("dtype", 9), _c("gpus", 4, True), _c("cols/gpu", 8, True),
+                        _c("bcast_ms", 10, True), _c("allgather_ms", 12, True)])
+        print(hdr)
+        print("-" * len(hdr))
+        for (sh, d, g, b, ag, w) in extra:
+            print(" ".join([_c(sh, 8), _c(d, 9), _c(str(g), 4, True), _c(str(w), 8, True),
+                            _c("%.4f" % b, 10, True), _c("-" if ag is None else "%.4f" % ag, 12, True)]))
+        print("ok")
+        sys.stdout.flush()
+    return 0
+
+
+def _c(t, w, right=False):
+    p = " " * max(0, w - len(t))
+    return p + t if right else t + p
+
+
+__all__ = ["main_sharded", "shard_plan", "table_line"]

@@ -1,0 +1,68 @@
+"""Multi-rank host logic on CPU: two gloo ranks run the same aggregation
+code that bench.py and the sharded CLI run over NCCL on GPUs."""
+import os
+import socket
+
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+from mlpgemm import dist_util as DU  # noqa: E402
+from mlpgemm.shard import shard_plan  # noqa: E402
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # each rank "timed" a different total; the job time is the slowest
+        total = 10.0 + 5.0 * rank
+        mx = DU.reduce_max(dist, total, "cpu")
+        ok = DU.reduce_all(dist, rank != 1 or True, "cpu")
+        bad = DU.reduce_all(dist, rank == 0, "cpu")     # one rank failed its check
+        rate = DU.weak_scaling_rate(2.0 * 4096 ** 3, world, 100, mx)
+        out[rank] = (mx, ok, bad, rate)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_aggregate():
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    for r in range(world):
+        mx, ok, bad, rate = out[r]
+        assert mx == 15.0
+        assert ok is True and bad is False
+        assert rate == pytest.approx(2.0 * 4096 ** 3 * 2 * 100 / 0.015 / 1e12)
+
+
+def test_shard_plan_covers_columns():
+    for M in (4096, 11008, 1000, 33):
+        for G in (1, 2, 4, 8):
+            plan = shard_plan(M, G)
+            assert len(plan) == G
+            assert sum(w for _, w in plan) == M
+            pos = 0
+            for m0, w in plan:
+                assert m0 == pos or w == 0
+                pos = m0 + w
+                if G > 1 and w and m0 + w < M:
+                    assert w % 32 == 0
+    assert shard_plan(11008, 8) == [(i * 1376, 1376) for i in range(8)]
+
+
+def test_strong_scaling_rate():
+    assert DU.strong_scaling_rate(2.0, 1.0) == pytest.approx(2e-9)
