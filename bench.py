@@ -8,8 +8,9 @@ Workload (default): the i8i8 -> int32 square GEMM, N = K = M = 4096, seeded
 int8 operands U{-127..127}, bit-exact against an int64 dot product.  A step
 is one GEMM.  W untimed warm-up steps, then exactly K timed steps, each
 bracketed by its own CUDA-event pair on the launching stream; a 256 MiB
-buffer (> the 126 MB L2) is overwritten before every timed step, outside
-the event pair, so every step starts with a cold L2.  Under torchrun each
+buffer (> the 126 MB L2) is read before every timed step, outside the
+event pair, so every step starts with a cold L2 (of clean lines: no dirty
+write-back competes with the timed GEMM).  Under torchrun each
 rank runs its own M-slice of a G-times wider GEMM (weak scaling, no data
 collective); the time is the max over ranks.
 
@@ -353,7 +354,7 @@ def ours(a):
         "config": {"workload": workload_name(dtype, N, K, M), "N": N, "K": K, "M": M,
                    "tile": tile, "per_gpu": f"each rank computes its own [{N},{M}] column block "
                                              f"of a [{N},{M * world}] output",
-                   "l2": "flushed: 256 MiB overwritten before every timed step, outside its events",
+                   "l2": "flushed: a 256 MiB buffer is read before every timed step, outside its events",
                    "operands": "seeded i.i.d. int8 U{-127..127}" if dtype == "i8i8" else "seeded",
                    "accumulate": "int32" if dtype == "i8i8" else "f32",
                    "parity": "bit-exact vs int64 dot product" if dtype == "i8i8" else "rel<=1e-3 vs fp64",

@@ -64,7 +64,7 @@ const char* kKernelNames[kNumDTypes] = {"fp16_mlp_gemm", "int8_mlp_gemm", "i8i8_
                                          "f8x4_mlp_gemm"};
 
 // ---- tile table -----------------------------------------------------------------
-enum TileKind { kTileTC = 0, kTileGemv = 1 };
+enum TileKind { kTileTC = 0, kTileGemv = 1, kTileStream = 2 };
 struct TileDef {
   const char* name;
   TileKind kind;
@@ -73,6 +73,7 @@ struct TileDef {
 };
 const TileDef kTiles[] = {
     {"256x256", kTileTC, 256, 256},  {"128x256", kTileTC, 256, 128}, {"128x128", kTileTC, 128, 128},
+    {"stream", kTileStream, 0, 0},
     {"gemv.k1", kTileGemv, 1, 0},    {"gemv.k2", kTileGemv, 2, 0},   {"gemv.k4", kTileGemv, 4, 0},
     {"gemv.k8", kTileGemv, 8, 0},    {"gemv.k16", kTileGemv, 16, 0}, {"gemv.k32", kTileGemv, 32, 0},
     {"gemv.k64", kTileGemv, 64, 0},
@@ -102,6 +103,7 @@ bool any_tc(int dt, int N, int K, int M) {
 bool tile_ok(int dt, int t, int N, int K, int M) {
   if (!valid_tile(t) || layout_check(dt, N, K, M) != GEMM_OK) return false;
   if (kTiles[t].kind == kTileTC) return tc_supported(dt, kTiles[t].bm, kTiles[t].param, N, K, M);
+  if (kTiles[t].kind == kTileStream) return stream_supported(dt, N, K, M);
   // CUDA-core tiles: the thin-row kernel, and the fallback where no
   // tensor-core tile covers the dtype or shape.
   return N <= 16 || !any_tc(dt, N, K, M);
@@ -145,6 +147,7 @@ int enqueue(DevState* s, int dt, int tile, const void* X, const void* W, void* Y
   a.num_sms = s->num_sms;
   cudaError_t e;
   if (kTiles[tile].kind == kTileTC) e = launch_tc(a, kTiles[tile].bm, kTiles[tile].param);
+  else if (kTiles[tile].kind == kTileStream) e = launch_stream(a);
   else e = launch_gemv(a, kTiles[tile].param);
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return GEMM_OK;
@@ -264,6 +267,7 @@ int gemm_default_tile(int dtype, int N, int K, int M) {
 size_t gemm_workspace_size(int dtype, int tile, int N, int K, int M) {
   if (!valid_tile(tile) || !valid_dtype(dtype)) return 0;
   if (kTiles[tile].kind == kTileTC) return tc_workspace(dtype, kTiles[tile].param, N, K, M);
+  if (kTiles[tile].kind == kTileStream) return stream_supported(dtype, N, K, M) ? stream_workspace(dtype, N, K, M) : 0;
   return gemv_workspace(dtype, kTiles[tile].param, N, K, M);
 }
 
@@ -364,7 +368,10 @@ int gemm_time(int device, int dtype, int tile, const void* X, const void* const*
     rc = enqueue(s, dtype, tile, X, Ws[i % nrot], Y, N, K, M, xscale, wscales ? wscales[i % nrot] : nullptr,
                  workspace, workspace_bytes, st);
   for (int i = 0; i < iters && rc == GEMM_OK; ++i) {
-    if (flush && flush_bytes) cudaMemsetAsync(flush, i & 0xFF, flush_bytes, st);
+    if (flush && flush_bytes) {
+      e = launch_l2_flush(flush, flush_bytes, s->num_sms, st);
+      if (e != cudaSuccess) { rc = cuda_fail(e, "L2 flush"); break; }
+    }
     const int r = (warmup + i) % nrot;
     cudaEventRecord(ev[2 * i], st);
     rc = enqueue(s, dtype, tile, X, Ws[r], Y, N, K, M, xscale, wscales ? wscales[r] : nullptr, workspace,

@@ -50,20 +50,72 @@ constexpr int w_bytes_x2() {
   return DT == kFP16 ? 4 : (DT == kF4F4 ? 1 : 2);
 }
 
-// Decode `E` weights from an aligned register chunk (raw bytes of one row).
-template <int DT, int E, int LW>
-__device__ __forceinline__ void decode_w_chunk(const uint32_t (&raw)[LW / 4], float (&w)[E]) {
-  const uint8_t* b = reinterpret_cast<const uint8_t*>(raw);
+// ---- exact widening to f16 pairs, and f16 x f16 -> f32 multiply-adds ----------
+// The products are formed by fma.rn.f32.f16 (f16 multiplicands, f32 addend):
+// an f16 x f16 product has at most 22 significant bits, so it is exact in
+// f32 and the accumulation is ordinary f32 -- no f16 rounding anywhere.
+
+// int8 x4 -> two f16x2 (exact): bias to unsigned, place each byte under the
+// exponent of 1024 (0x64xx = 1024 + byte), subtract 1152.
+__device__ __forceinline__ void i8x4_to_h2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  const uint32_t a = v ^ 0x80808080u;
+  uint32_t t0 = __byte_perm(a, 0x64646464u, 0x4140), t1 = __byte_perm(a, 0x64646464u, 0x4342);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(t0), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(t1), "r"(0x64806480u));
+}
+
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"((unsigned short)two));
+  return d;
+}
+
+// 8 E2M1 (low nibble first) -> 4 f16x2
+__device__ __forceinline__ void e2m1x8_to_h2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+// a0 += w.lo * x ; a1 += w.hi * x   (one activation, two weight columns)
+__device__ __forceinline__ void fma2_bcast(float& a0, float& a1, uint32_t w2, unsigned short x) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "fma.rn.f32.f16 %0, l, %3, %0;\n\tfma.rn.f32.f16 %1, h, %3, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(w2), "h"(x));
+}
+
+// a += w.lo * x.lo + w.hi * x.hi   (two consecutive K elements)
+__device__ __forceinline__ void fma2_dot(float& a, uint32_t w2, uint32_t x2) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\tmov.b32 {wl, wh}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+      "fma.rn.f32.f16 %0, wl, xl, %0;\n\tfma.rn.f32.f16 %0, wh, xh, %0;\n\t}"
+      : "+f"(a)
+      : "r"(w2), "r"(x2));
+}
+
+// Widen one thread's weight chunk (LW bytes of one [K,M] row) to f16 pairs.
+template <int DT, int LW>
+__device__ __forceinline__ void widen_chunk(const uint32_t (&raw)[LW / 4],
+                                            uint32_t (&h)[LW * 2 / w_bytes_x2<DT>() / 2]) {
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
+  for (int i = 0; i < LW / 4; ++i) {
     if constexpr (DT == kFP16) {
-      w[j] = dec_f16(reinterpret_cast<const uint16_t*>(raw)[j]);
-    } else if constexpr (w_is_i8(DT)) {
-      w[j] = (float)(int8_t)b[j];
+      h[i] = raw[i];
+    } else if constexpr (DT == kINT8) {
+      i8x4_to_h2(raw[i], h[2 * i], h[2 * i + 1]);
     } else if constexpr (w_is_e4m3(DT)) {
-      w[j] = dec_e4m3(b[j]);
-    } else {  // f4f4, packed along M, low nibble = even column
-      w[j] = dec_e2m1((j & 1) ? (b[j >> 1] >> 4) : (b[j >> 1] & 0xF));
+      h[2 * i] = e4m3x2_to_h2(raw[i]);
+      h[2 * i + 1] = e4m3x2_to_h2(raw[i] >> 16);
+    } else {   // f4f4
+      uint32_t q[4];
+      e2m1x8_to_h2(raw[i], q);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[4 * i + j] = q[j];
     }
   }
 }
@@ -127,33 +179,41 @@ __device__ __forceinline__ void finish_tile(const GemvParams& p, Acc* red, int n
 // ---------------------------------------------------------------------------
 // [K,M] weights
 // ---------------------------------------------------------------------------
-template <int DT, int NR, int LW>
+// A CTA owns a slab of CL x LW bytes of columns (CL lanes side by side on
+// one row) and the K range of its split; its 256/CL row-lanes walk that
+// range with stride 256/CL rows, 8 rows in flight per thread.  Activations
+// sit in shared memory as f16 (exact for half, E4M3 and E2M1 inputs), or
+// int8 for i8i8.  The row-lanes are reduced in shared memory in a fixed
+// order, the K splits through the workspace (finish_tile).
+template <int DT, int NR, int LW, int CL>
 __global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
   using Acc = std::conditional_t<DT == kI8I8, int, float>;
-  constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights per thread
-  constexpr int CPC = 32 * E;                   // columns per CTA
+  constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights (columns) per thread
+  constexpr int CPC = CL * E;                   // columns per CTA
+  constexpr int H = E / 2;                      // f16 pairs per thread
+  constexpr int RL = kThreads / CL;             // row-lanes
+  constexpr int U = 8;                          // rows in flight per thread
+  static_assert(DT != kI8I8 || U % 4 == 0, "dp4a takes groups of 4 rows");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Acc* xs = reinterpret_cast<Acc*>(smem_raw);   // [NR][kchunk]
-  const int kc = p.kchunk;
-  Acc* red = xs + NR * kc;                      // [NR][CPC]
+  const int kc = p.kchunk;                      // multiple of 32
+  unsigned char* xsb = smem_raw;                // [NR][kc] f16 (or int8)
+  Acc* red = reinterpret_cast<Acc*>(smem_raw + (size_t)NR * kc * 2);   // [RL][NR][CPC]
 
   const int m0 = blockIdx.x * CPC;
   const int kb = blockIdx.y * kc;
   const int ke = min(p.K, kb + kc);
   const int n0 = blockIdx.z * NR;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
+  const int cl = tid % CL, rl = tid / CL;
 
   for (int i = tid; i < NR * kc; i += kThreads) {
     const int n = i / kc, k = kb + i % kc;
-    Acc v = 0;
-    if (n0 + n < p.N && k < ke) {
-      if constexpr (DT == kI8I8) {
-        v = reinterpret_cast<const int8_t*>(p.X)[(size_t)(n0 + n) * p.K + k];
-      } else {
-        v = load_x<DT>(p.X, p.xscale, n0 + n, k, p.K);
-      }
+    const bool in = n0 + n < p.N && k < ke;
+    if constexpr (DT == kI8I8) {
+      reinterpret_cast<int8_t*>(xsb)[i] = in ? reinterpret_cast<const int8_t*>(p.X)[(size_t)(n0 + n) * p.K + k] : 0;
+    } else {
+      reinterpret_cast<__half*>(xsb)[i] = __float2half_rn(in ? load_x<DT>(p.X, p.xscale, n0 + n, k, p.K) : 0.f);
     }
-    xs[i] = v;
   }
   __syncthreads();
 
@@ -163,47 +223,71 @@ __global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
 #pragma unroll
     for (int j = 0; j < E; ++j) acc[n][j] = 0;
 
-  const int mc = m0 + lane * E;  // first column owned by this thread
-  const size_t row_bytes_x2 = (size_t)p.M * w_bytes_x2<DT>();
-  const bool vec = (mc + E <= p.M) && ((row_bytes_x2 / 2) % LW == 0) && (row_bytes_x2 % 2 == 0);
+  const int mc = m0 + cl * E;   // first column owned by this thread
+  const size_t rb = (size_t)p.M * w_bytes_x2<DT>() / 2;   // bytes per weight row
+  const bool vec = (mc + E <= p.M) && ((size_t)p.M * w_bytes_x2<DT>() % 2 == 0) && (rb % LW == 0);
   const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.W) + (size_t)mc * w_bytes_x2<DT>() / 2;
 
   if (vec) {
-#pragma unroll 4
-    for (int k = kb + warp; k < ke; k += kWarps) {
-      uint32_t raw[LW / 4];
-      const uint8_t* src = wbase + (size_t)k * (row_bytes_x2 / 2);
-      if constexpr (LW == 16) {
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
-        raw[0] = v.x; raw[1] = v.y; raw[2] = v.z; raw[3] = v.w;
-      } else if constexpr (LW == 8) {
-        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
-        raw[0] = v.x; raw[1] = v.y;
-      } else {
-        raw[0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
+    // rows k = kb + U*rl*... : row-lane rl takes rows kb + U*rl + i (i < U), then jumps by U*RL
+    for (int k0 = kb + U * rl; k0 < ke; k0 += U * RL) {
+      uint32_t raw[U][LW / 4];
+#pragma unroll
+      for (int r = 0; r < U; ++r) {
+        const int k = k0 + r;
+        if (k < ke) {
+          const uint8_t* src = wbase + (size_t)k * rb;
+          if constexpr (LW == 16) {
+            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
+            raw[r][0] = v.x; raw[r][1] = v.y; raw[r][2] = v.z; raw[r][3] = v.w;
+          } else if constexpr (LW == 8) {
+            const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
+            raw[r][0] = v.x; raw[r][1] = v.y;
+          } else {
+            raw[r][0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < LW / 4; ++q) raw[r][q] = 0;
+        }
       }
-      const int kl = k - kb;
+      const int kl = k0 - kb;
       if constexpr (DT == kI8I8) {
-        const int8_t* b = reinterpret_cast<const int8_t*>(raw);
+        // 4x4 byte transposes, then dp4a over 4 K rows at a time
 #pragma unroll
-        for (int n = 0; n < NR; ++n) {
-          const int xv = xs[n * kc + kl];
+        for (int g = 0; g < U / 4; ++g) {
 #pragma unroll
-          for (int j = 0; j < E; ++j) acc[n][j] += xv * (int)b[j];
+          for (int n = 0; n < NR; ++n) {
+            const int x4 = *reinterpret_cast<const int*>(xsb + (size_t)n * kc + kl + 4 * g);
+#pragma unroll
+            for (int c = 0; c < LW / 4; ++c) {
+              const uint32_t lo01 = __byte_perm(raw[4 * g][c], raw[4 * g + 1][c], 0x5140);
+              const uint32_t hi01 = __byte_perm(raw[4 * g][c], raw[4 * g + 1][c], 0x7362);
+              const uint32_t lo23 = __byte_perm(raw[4 * g + 2][c], raw[4 * g + 3][c], 0x5140);
+              const uint32_t hi23 = __byte_perm(raw[4 * g + 2][c], raw[4 * g + 3][c], 0x7362);
+              acc[n][4 * c + 0] = __dp4a((int)__byte_perm(lo01, lo23, 0x5410), x4, acc[n][4 * c + 0]);
+              acc[n][4 * c + 1] = __dp4a((int)__byte_perm(lo01, lo23, 0x7632), x4, acc[n][4 * c + 1]);
+              acc[n][4 * c + 2] = __dp4a((int)__byte_perm(hi01, hi23, 0x5410), x4, acc[n][4 * c + 2]);
+              acc[n][4 * c + 3] = __dp4a((int)__byte_perm(hi01, hi23, 0x7632), x4, acc[n][4 * c + 3]);
+            }
+          }
         }
       } else {
-        float w[E];
-        decode_w_chunk<DT, E, LW>(raw, w);
 #pragma unroll
-        for (int n = 0; n < NR; ++n) {
-          const float xv = xs[n * kc + kl];
+        for (int r = 0; r < U; ++r) {
+          uint32_t h[H];
+          widen_chunk<DT, LW>(raw[r], h);
 #pragma unroll
-          for (int j = 0; j < E; ++j) acc[n][j] = fmaf(xv, w[j], acc[n][j]);
+          for (int n = 0; n < NR; ++n) {
+            const unsigned short xv = reinterpret_cast<const unsigned short*>(xsb)[(size_t)n * kc + kl + r];
+#pragma unroll
+            for (int j = 0; j < H; ++j) fma2_bcast(acc[n][2 * j], acc[n][2 * j + 1], h[j], xv);
+          }
         }
       }
     }
   } else {
-    for (int k = kb + warp; k < ke; k += kWarps) {
+    for (int k = kb + rl; k < ke; k += RL) {
       const int kl = k - kb;
 #pragma unroll
       for (int j = 0; j < E; ++j) {
@@ -212,53 +296,80 @@ __global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
         if constexpr (DT == kI8I8) {
           const int wv = reinterpret_cast<const int8_t*>(p.W)[(size_t)k * p.M + m];
 #pragma unroll
-          for (int n = 0; n < NR; ++n) acc[n][j] += xs[n * kc + kl] * wv;
+          for (int n = 0; n < NR; ++n) acc[n][j] += (int)reinterpret_cast<const int8_t*>(xsb)[(size_t)n * kc + kl] * wv;
         } else {
           const float wv = load_w_mn<DT>(p.W, k, m, p.M);
 #pragma unroll
-          for (int n = 0; n < NR; ++n) acc[n][j] = fmaf(xs[n * kc + kl], wv, acc[n][j]);
+          for (int n = 0; n < NR; ++n)
+            acc[n][j] = fmaf(__half2float(reinterpret_cast<const __half*>(xsb)[(size_t)n * kc + kl]), wv, acc[n][j]);
         }
       }
     }
   }
 
-  // cross-warp reduction in a fixed order (warp 0 first)
-  for (int w = 0; w < kWarps; ++w) {
-    if (warp == w) {
+  // row-lane reduction in a fixed order: red[rl][n][col], then column sums
 #pragma unroll
-      for (int n = 0; n < NR; ++n)
+  for (int n = 0; n < NR; ++n)
 #pragma unroll
-        for (int j = 0; j < E; ++j) {
-          Acc* r = &red[n * CPC + lane * E + j];
-          *r = (w == 0) ? acc[n][j] : (*r + acc[n][j]);
-        }
-    }
-    __syncthreads();
+    for (int j = 0; j < E; ++j) red[((size_t)rl * NR + n) * CPC + cl * E + j] = acc[n][j];
+  __syncthreads();
+  Acc* out = red;   // the sums overwrite row-lane 0's slice, which thread t reads first
+  for (int i = tid; i < NR * CPC; i += kThreads) {
+    Acc sum = 0;
+    for (int q = 0; q < RL; ++q) sum += red[(size_t)q * NR * CPC + i];
+    out[i] = sum;   // only row-lane 0's entry i is overwritten, after it was read
   }
-  finish_tile<Acc>(p, red, n0, NR, m0, CPC);
+  __syncthreads();
+  finish_tile<Acc>(p, out, n0, NR, m0, CPC);
 }
 
 // ---------------------------------------------------------------------------
 // [M,K] weights (mxfp4 family): E2M1 packed along K, UE8M0 [M, K/32]
 // ---------------------------------------------------------------------------
+// Each 16-byte load is one 32-element block with one W scale (and, for
+// mxfp4/a4 and mxfp4/a8, one X scale per row): the block's dot product of
+// the unscaled f16 values is formed exactly in f32 and then multiplied by
+// 2^(sw-127) * 2^(sx-127).
 template <int DT, int NR>
 __global__ void __launch_bounds__(kThreads) gemv_km_kernel(GemvParams p) {
   constexpr int RPW = 4;              // output columns per warp
   constexpr int CPC = kWarps * RPW;   // 32 columns per CTA
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* xs = reinterpret_cast<float*>(smem_raw);  // [NR][kchunk]
-  const int kc = p.kchunk;
-  float* red = xs + NR * kc;                       // [NR][CPC]
+  const int kc = p.kchunk;            // multiple of 32
+  __half* xs = reinterpret_cast<__half*>(smem_raw);                       // [NR][kc] unscaled
+  float* xsc = reinterpret_cast<float*>(smem_raw + (size_t)NR * kc * 2);   // [NR][kc/32]
+  float* red = xsc + NR * (kc / 32);                                       // [NR][CPC]
 
   const int m0 = blockIdx.x * CPC;
   const int kb = blockIdx.y * kc;
   const int ke = min(p.K, kb + kc);
   const int n0 = blockIdx.z * NR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kbpr = p.K / 32;
 
   for (int i = tid; i < NR * kc; i += kThreads) {
     const int n = i / kc, k = kb + i % kc;
-    xs[i] = (n0 + n < p.N && k < ke) ? load_x<DT>(p.X, p.xscale, n0 + n, k, p.K) : 0.f;
+    float v = 0.f;
+    if (n0 + n < p.N && k < ke) {
+      const size_t xi = (size_t)(n0 + n) * p.K + k;
+      if constexpr (x_is_half(DT)) {
+        v = dec_f16(reinterpret_cast<const uint16_t*>(p.X)[xi]);
+      } else if constexpr (x_is_e4m3(DT)) {
+        v = dec_e4m3(reinterpret_cast<const uint8_t*>(p.X)[xi]);
+      } else {
+        const uint8_t byte = reinterpret_cast<const uint8_t*>(p.X)[xi >> 1];
+        v = dec_e2m1((xi & 1) ? (byte >> 4) : (byte & 0xF));
+      }
+    }
+    xs[i] = __float2half_rn(v);   // exact: half, E4M3 and E2M1 values are f16 values
+  }
+  for (int i = tid; i < NR * (kc / 32); i += kThreads) {
+    const int n = i / (kc / 32), blk = kb / 32 + i % (kc / 32);
+    float sc = 1.f;
+    if constexpr (x_scaled(DT)) {
+      if (n0 + n < p.N && blk < kbpr) sc = dec_ue8m0(p.xscale[(size_t)(n0 + n) * kbpr + blk]);
+    }
+    xsc[i] = sc;
   }
   __syncthreads();
 
@@ -269,55 +380,56 @@ __global__ void __launch_bounds__(kThreads) gemv_km_kernel(GemvParams p) {
     for (int r = 0; r < RPW; ++r) acc[n][r] = 0.f;
 
   const int kblocks = (ke - kb) / 32;  // kchunk and K are multiples of 32
-  const int kbpr = p.K / 32;           // scale bytes per weight row
   const uint8_t* W = reinterpret_cast<const uint8_t*>(p.W);
-  for (int blk = lane; blk < kblocks; blk += 32) {
-    const int k = kb + blk * 32;
-    uint4 wv[RPW];
-    float sc[RPW];
+  constexpr int BPL = 4;               // blocks per lane in flight, per row
+  for (int b0 = lane; b0 < kblocks; b0 += 32 * BPL) {
+    uint4 wv[BPL][RPW];
+    float sc[BPL][RPW];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int m = m0 + warp * RPW + r;
-      if (m < p.M) {
-        wv[r] = __ldcs(reinterpret_cast<const uint4*>(W + ((size_t)m * p.K + k) / 2));
-        sc[r] = dec_ue8m0(p.wscale[(size_t)m * kbpr + k / 32]);
-      } else {
-        wv[r] = make_uint4(0, 0, 0, 0);
-        sc[r] = 0.f;
-      }
-    }
-    float d[NR][RPW];
+    for (int t = 0; t < BPL; ++t) {
+      const int blk = b0 + 32 * t;
 #pragma unroll
-    for (int n = 0; n < NR; ++n)
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) d[n][r] = 0.f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {        // 4 words x 8 nibbles
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {      // 4 elements at a time
-        float4 xv[NR];
-#pragma unroll
-        for (int n = 0; n < NR; ++n)
-          xv[n] = *reinterpret_cast<const float4*>(&xs[n * kc + blk * 32 + q * 8 + h * 4]);
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          const uint32_t word = (&wv[r].x)[q] >> (16 * h);
-          const float w0 = dec_e2m1(word), w1 = dec_e2m1(word >> 4);
-          const float w2 = dec_e2m1(word >> 8), w3 = dec_e2m1(word >> 12);
-#pragma unroll
-          for (int n = 0; n < NR; ++n) {
-            d[n][r] = fmaf(xv[n].x, w0, d[n][r]);
-            d[n][r] = fmaf(xv[n].y, w1, d[n][r]);
-            d[n][r] = fmaf(xv[n].z, w2, d[n][r]);
-            d[n][r] = fmaf(xv[n].w, w3, d[n][r]);
-          }
+      for (int r = 0; r < RPW; ++r) {
+        const int m = m0 + warp * RPW + r;
+        if (m < p.M && blk < kblocks) {
+          const int k = kb + blk * 32;
+          wv[t][r] = __ldcs(reinterpret_cast<const uint4*>(W + ((size_t)m * p.K + k) / 2));
+          sc[t][r] = dec_ue8m0(__ldg(p.wscale + (size_t)m * kbpr + k / 32));
+        } else {
+          wv[t][r] = make_uint4(0, 0, 0, 0);
+          sc[t][r] = 0.f;
         }
       }
     }
 #pragma unroll
-    for (int n = 0; n < NR; ++n)
+    for (int t = 0; t < BPL; ++t) {
+      const int blk = b0 + 32 * t;
+      if (blk >= kblocks) break;
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) acc[n][r] = fmaf(d[n][r], sc[r], acc[n][r]);
+      for (int n = 0; n < NR; ++n) {
+        const uint4* xq = reinterpret_cast<const uint4*>(xs + (size_t)n * kc + blk * 32);
+        uint32_t x2[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = xq[q];
+          x2[4 * q] = v.x; x2[4 * q + 1] = v.y; x2[4 * q + 2] = v.z; x2[4 * q + 3] = v.w;
+        }
+        const float xsn = xsc[n * (kc / 32) + blk];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          float d = 0.f;
+          const uint32_t words[4] = {wv[t][r].x, wv[t][r].y, wv[t][r].z, wv[t][r].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t h[4];
+            e2m1x8_to_h2(words[q], h);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) fma2_dot(d, h[j], x2[4 * q + j]);
+          }
+          acc[n][r] = fmaf(d, sc[t][r] * xsn, acc[n][r]);
+        }
+      }
+    }
   }
   // butterfly reduction across lanes (same order on every run)
 #pragma unroll
@@ -348,6 +460,11 @@ constexpr bool is_kmajor() { return w_is_mx(DT); }
 // Rows per CTA: 1, 2, 4 or 8 (larger N uses several row blocks).
 inline int pick_nr(int N) { return N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8; }
 
+// Lanes side by side on one weight row ([K,M] kernel): a narrow slab gives
+// enough CTAs without splitting K; wide slabs for many rows (N > 1 runs are
+// compute-heavier and prefer fewer, wider CTAs).
+constexpr int kLanesPerRow = 4;
+
 // Bytes loaded per thread per weight row, so that NR * E <= 64 accumulators.
 template <int DT>
 constexpr int pick_lw(int NR) {
@@ -363,7 +480,7 @@ int cols_per_cta(int dt, int N) {
   const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
   int lw = 16;
   while (lw > 4 && nr * (lw * 2 / bx2) > 64) lw /= 2;
-  return 32 * (lw * 2 / bx2);
+  return kLanesPerRow * (lw * 2 / bx2);
 }
 
 // Workspace layout: [kCounterBytes of tile counters][ksplit * N * M partials].
@@ -381,15 +498,16 @@ template <int DT, int NR>
 cudaError_t launch_nr(const GemvParams& p, dim3 grid, cudaStream_t st) {
   size_t smem;
   if constexpr (is_kmajor<DT>()) {
-    smem = (size_t)NR * p.kchunk * 4 + (size_t)NR * 32 * 4;
+    smem = (size_t)NR * p.kchunk * 2 + (size_t)NR * (p.kchunk / 32) * 4 + (size_t)NR * 32 * 4;
     auto k = gemv_km_kernel<DT, NR>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, st>>>(p);
   } else {
     constexpr int LW = pick_lw<DT>(NR);
     constexpr int E = LW * 2 / w_bytes_x2<DT>();
-    smem = (size_t)NR * p.kchunk * 4 + (size_t)NR * 32 * E * 4;
-    auto k = gemv_mn_kernel<DT, NR, LW>;
+    constexpr int CL = kLanesPerRow;
+    smem = (size_t)NR * p.kchunk * 2 + (size_t)(kThreads / CL) * NR * CL * E * 4;
+    auto k = gemv_mn_kernel<DT, NR, LW, CL>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k<<<grid, kThreads, smem, st>>>(p);
   }
@@ -407,6 +525,21 @@ cudaError_t launch_dt(const GemvParams& p, dim3 grid, int nr, cudaStream_t st) {
 }
 
 }  // namespace
+
+__global__ void __launch_bounds__(512) l2_flush_kernel(const uint4* __restrict__ buf, size_t n16,
+                                                       unsigned* __restrict__ never) {
+  uint32_t x = 0;
+  for (size_t i = blockIdx.x * 512ull + threadIdx.x; i < n16; i += (size_t)gridDim.x * 512ull) {
+    const uint4 v = __ldcg(buf + i);
+    x ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (x == 0x9E3779B9u && never) *never = x;   // keeps the loads; never taken for a zero buffer
+}
+
+cudaError_t launch_l2_flush(const void* buf, size_t bytes, int num_sms, cudaStream_t st) {
+  l2_flush_kernel<<<4 * num_sms, 512, 0, st>>>(static_cast<const uint4*>(buf), bytes / 16, nullptr);
+  return cudaGetLastError();
+}
 
 int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {
   const int nr = pick_nr(N);

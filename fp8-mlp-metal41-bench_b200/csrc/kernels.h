@@ -27,12 +27,22 @@ int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms);
 size_t gemv_workspace(int dt, int ksplit, int N, int K, int M);
 cudaError_t launch_gemv(const RunArgs& a, int ksplit);
 
+// ---- persistent TMA-streaming GEMV (thin rows, N <= 16) -------------------------
+bool stream_supported(int dt, int N, int K, int M);
+size_t stream_workspace(int dt, int N, int K, int M);
+cudaError_t launch_stream(const RunArgs& a);
+
 // ---- tcgen05 tensor-core GEMM --------------------------------------------------
 // bm: 128 (one CTA per tile) or 256 (a CTA pair, cta_group::2); bn: 128 or 256.
 bool tc_supported(int dt, int bm, int bn, int N, int K, int M);
 size_t tc_workspace(int dt, int bn, int N, int K, int M);
 int tc_launches(int dt);
 cudaError_t launch_tc(const RunArgs& a, int bm, int bn);
+
+// Read `bytes` of `buf` (a buffer larger than L2) so that L2 holds only clean
+// lines of it afterwards: a cold cache for the next kernel, without the dirty
+// write-back a memset would leave behind (defined in gemv.cu).
+cudaError_t launch_l2_flush(const void* buf, size_t bytes, int num_sms, cudaStream_t st);
 
 // Record a message for gemm_last_error() (defined in api.cu).
 void set_last_error(const char* msg);

@@ -145,8 +145,9 @@ int gemm_sync(int device, void *stream);
  * Ws / wscales are arrays of `nrot` weight copies used round-robin, so that
  * weights smaller than L2 still stream from HBM every iteration (nrot = 1:
  * the reference's behaviour).  If `flush` is non-NULL, `flush_bytes` of it
- * are overwritten before every timed iteration, outside its event pair, so
- * each timed GEMM starts with a cold L2.  ms_out receives `iters` times. */
+ * (more than the 126 MB L2) are read before every timed iteration, outside
+ * its event pair, so each timed GEMM starts with an L2 holding only clean
+ * lines of that buffer.  ms_out receives `iters` times. */
 int gemm_time(int device, int dtype, int tile, const void *X, const void *const *Ws, void *Y,
               int N, int K, int M, const void *xscale, const void *const *wscales, int nrot,
               void *workspace, size_t workspace_bytes, int warmup, int iters,

@@ -139,3 +139,23 @@ def test_rejects_bad_layout(gemm):
     with pytest.raises(G.GemmError) as e:
         G.run(0, dt, G.tile_index("gemv.k1"), 1, 1, 1, 4, 96, 8, 1, 1)
     assert e.value.code == G.GEMM_ERR_ARGS
+
+
+@pytest.mark.parametrize("dtype", F.DTYPES)
+@pytest.mark.parametrize("shape", [(1, 4096, 11008), (3, 1024, 1008), (16, 512, 640)])
+def test_stream_thin_rows(gemm, dtype, shape):
+    # persistent TMA-streaming kernel (stream-K split, cross-CTA reduction)
+    N, K, M = shape
+    if dtype in F.W_MX:
+        K = max(K, 512)
+    ti = gemm.tile_index("stream")
+    if not gemm.tile_supported(F.CODE[dtype], ti, N, K, M):
+        pytest.skip("register or shared-memory budget")
+    out, ref, _ = run_case(gemm, dtype, "stream", N, K, M)
+    assert_close(dtype, out, ref)
+
+
+def test_stream_deterministic(gemm):
+    a, ref, ops = run_case(gemm, "int8", "stream", 1, 4096, 11008)
+    b, _, _ = run_case(gemm, "int8", "stream", 1, 4096, 11008, ops=ops)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
