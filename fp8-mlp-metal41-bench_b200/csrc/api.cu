@@ -106,6 +106,7 @@ bool tile_ok(int dt, int t, int N, int K, int M) {
   if (kTiles[t].kind == kTileStream) return stream_supported(dt, N, K, M);
   // CUDA-core tiles: the thin-row kernel, and the fallback where no
   // tensor-core tile covers the dtype or shape.
+  if (!gemv_supported(dt, kTiles[t].param, N, K, M)) return false;
   return N <= 16 || !any_tc(dt, N, K, M);
 }
 

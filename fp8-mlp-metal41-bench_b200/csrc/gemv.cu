@@ -4,25 +4,28 @@
 // The reference serves N = 1 with its smallest Metal tiles (defaultTile,
 // main.swift:148-154: 16x32 for N <= 16).  Here thin rows get a kernel of
 // their own: the weights are streamed from HBM once with 128-bit coalesced
-// loads, decoded in registers, multiplied by activations held in shared
-// memory (decoded to f32 once per CTA), reduced across warps in shared
-// memory and across K-splits through a caller-provided workspace.  The last
-// CTA of each output tile to finish sums the K-split partials in a fixed
-// order, so results are deterministic (and exact for i8i8).
+// loads (128 contiguous bytes per row and warp instruction), two register
+// buffers deep, decoded in registers and multiplied by activations held in
+// shared memory.  Partial sums are reduced with warp shuffles, across warps in
+// shared memory and across K splits either inside a thread-block cluster
+// (up to 8 splits, through distributed shared memory) or, for more splits,
+// through a caller-provided workspace where the last CTA of each output tile
+// sums the partials.  Every reduction runs in a fixed order, so results are
+// deterministic (and exact for i8i8).
 //
 // Two weight layouts:
 //   [K,M] "MN-major" (fp16, int8, i8i8, fp8, f8f8, f4f4): a thread owns a
-//        16/8/4-byte run of one weight row (8..32 columns); the 8 warps of
-//        a CTA walk interleaved K rows.
-//   [M,K] "K-major" (the mxfp4 family): a warp owns 4 output columns; each
-//        lane takes 16-byte blocks of 32 E2M1 values (one UE8M0 scale each)
-//        and the warp reduces with shuffles.
+//        16/8/4-byte run of one weight row (8..32 columns) and walks groups
+//        of 4 consecutive rows of its K split.
+//   [M,K] "K-major" (the mxfp4 family): 8 lanes share one weight row and
+//        take its 16-byte blocks of 32 E2M1 values (one UE8M0 scale each).
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <type_traits>
 
 #include "formats.cuh"
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace mlpg {
 
@@ -42,7 +45,28 @@ struct GemvParams {
   int kchunk;           // K elements per split (multiple of 32)
   void* part;           // [ksplit][N][M] partial sums (float, or int32 for i8i8)
   unsigned* counters;   // one per (row block, column block)
+  int cluster;          // K splits form a thread-block cluster (ksplit <= 8)
+  int stream;           // persistent stream-K mode (below)
+  // persistent stream-K mode: gridDim.x CTAs take equal contiguous runs of
+  // units (one CTA-wide row group of one column slab) in slab-major order
+  int nslabs;           // column slabs of CPC columns
+  int units_per_slab;
+  int total_units;
 };
+
+// contiguous unit range of CTA c of G (stream-K)
+__device__ __forceinline__ void cta_range(int c, int G, int U, int& u0, int& u1) {
+  u0 = (int)((long long)c * U / G);
+  u1 = (int)((long long)(c + 1) * U / G);
+}
+
+// first CTA whose range contains unit u
+__device__ __forceinline__ int owner_of(int u, int G, int U) {
+  int c = (int)(((long long)u * G + G - 1) / U);   // largest c with c*U/G <= u
+  while (c > 0 && (long long)c * U / G > u) --c;
+  while ((long long)(c + 1) * U / G <= u) ++c;
+  return c;
+}
 
 // Bytes per weight element, times two (FP4 packs two per byte).
 template <int DT>
@@ -134,7 +158,7 @@ __device__ __forceinline__ float load_w_mn(const void* W, int k, int m, int M) {
 }
 
 template <typename Acc>
-__device__ __forceinline__ void finish_tile(const GemvParams& p, Acc* red, int n0, int NR,
+__device__ __forceinline__ void finish_tile(const GemvParams& p, const Acc* red, int n0, int NR,
                                             int m0, int CPC) {
   // red[NR][CPC] holds this CTA's (row block, column block, K split) result.
   const int tid = threadIdx.x;
@@ -176,36 +200,152 @@ __device__ __forceinline__ void finish_tile(const GemvParams& p, Acc* red, int n
   if (tid == 0) p.counters[tile] = 0u;  // ready for the next launch
 }
 
+// K splits that form one thread-block cluster (cluster dims 1 x ksplit x 1,
+// so the cluster rank is the split index): every CTA's reduced tile stays in
+// its own shared memory; after a cluster barrier CTA r sums its share of the
+// tile over the CTAs of the cluster, in rank order, through distributed shared
+// memory and writes Y.  No workspace, no atomics, deterministic.
+template <typename Acc>
+__device__ __forceinline__ void cluster_reduce(const GemvParams& p, const Acc* red, int n0, int NR,
+                                               int m0, int CPC) {
+  cluster_sync();   // release/acquire: every CTA's tile is complete and visible
+  const int cs = p.ksplit;
+  const int rank = (int)cluster_ctarank();
+  const int tot = NR * CPC;
+  const int share = (tot + cs - 1) / cs;
+  const int i0 = rank * share, i1 = min(tot, i0 + share);
+  Acc* Y = reinterpret_cast<Acc*>(p.Y);
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += kThreads) {
+    Acc s = 0;
+    for (int q = 0; q < cs; ++q) {
+      const uint32_t v = ld_dsmem_u32(mapa_shared(red + i, (uint32_t)q));
+      if constexpr (std::is_same_v<Acc, int>) s += (int)v;
+      else s += __uint_as_float(v);
+    }
+    const int n = n0 + i / CPC, m = m0 + i % CPC;
+    if (n < p.N && m < p.M) Y[(size_t)n * p.M + m] = s;
+  }
+  cluster_sync();   // no CTA leaves while a peer may still read its shared memory
+}
+
+template <typename Acc>
+__device__ __forceinline__ void reduce_splits(const GemvParams& p, const Acc* red, int n0, int NR,
+                                              int m0, int CPC) {
+  if (p.cluster) cluster_reduce<Acc>(p, red, n0, NR, m0, CPC);
+  else finish_tile<Acc>(p, red, n0, NR, m0, CPC);
+}
+
+// Stream-K: emit this CTA's reduced piece red[NR][CPC] of `slab`.  A slab
+// held by one CTA goes straight to Y; a shared slab's pieces go to partial
+// slots (slot slab + c is unique: the CTAs sharing a slab are consecutive),
+// and the last of its CTAs to arrive sums them in CTA order.  Workspace:
+// [64 KB counters: row block x slab][slots: row block x (nslabs + G) x NR x CPC].
+template <typename Acc>
+__device__ __forceinline__ void stream_emit(const GemvParams& p, const Acc* red, int slab, int n0,
+                                            int NR, int CPC) {
+  __shared__ int s_last_piece;
+  const int tid = threadIdx.x, G = gridDim.x, c = blockIdx.x;
+  const int first = owner_of(slab * p.units_per_slab, G, p.total_units);
+  const int last = owner_of((slab + 1) * p.units_per_slab - 1, G, p.total_units);
+  const int m0 = slab * CPC;
+  Acc* Y = reinterpret_cast<Acc*>(p.Y);
+  if (first == last) {
+    for (int i = tid; i < NR * CPC; i += kThreads) {
+      const int n = n0 + i / CPC, m = m0 + i % CPC;
+      if (n < p.N && m < p.M) Y[(size_t)n * p.M + m] = red[i];
+    }
+  } else {
+    const size_t rowblk = blockIdx.z;
+    Acc* base = reinterpret_cast<Acc*>(p.part) + rowblk * (size_t)(p.nslabs + G) * NR * CPC;
+    Acc* slot = base + (size_t)(slab + c) * NR * CPC;
+    for (int i = tid; i < NR * CPC; i += kThreads) slot[i] = red[i];
+    __threadfence();
+    __syncthreads();
+    unsigned* ctr = p.counters + rowblk * p.nslabs + slab;
+    if (tid == 0) s_last_piece = atomicAdd(ctr, 1u) == (unsigned)(last - first);
+    __syncthreads();
+    if (s_last_piece) {
+      __threadfence();
+      for (int i = tid; i < NR * CPC; i += kThreads) {
+        const int n = n0 + i / CPC, m = m0 + i % CPC;
+        if (n >= p.N || m >= p.M) continue;
+        Acc sum = 0;
+        for (int q = first; q <= last; ++q) sum += __ldcg(base + (size_t)(slab + q) * NR * CPC + i);
+        Y[(size_t)n * p.M + m] = sum;
+      }
+      if (tid == 0) *ctr = 0u;   // ready for the next launch
+    }
+  }
+  __syncthreads();   // the scratch is reused by the next piece
+}
+
 // ---------------------------------------------------------------------------
 // [K,M] weights
 // ---------------------------------------------------------------------------
-// A CTA owns a slab of CL x LW bytes of columns (CL lanes side by side on
-// one row) and the K range of its split; its 256/CL row-lanes walk that
-// range with stride 256/CL rows, 8 rows in flight per thread.  Activations
-// sit in shared memory as f16 (exact for half, E4M3 and E2M1 inputs), or
-// int8 for i8i8.  The row-lanes are reduced in shared memory in a fixed
-// order, the K splits through the workspace (finish_tile).
-template <int DT, int NR, int LW, int CL>
-__global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
+// A CTA owns a slab of CL x LW contiguous bytes of every weight row (CL
+// lanes side by side: 128 bytes for LW = 16) and the K range of its split.
+// Its 256/CL row-lanes take groups of U consecutive rows, RL groups apart.
+// The loads of the first group go out before the activations are staged, and
+// every group's loads are issued before the previous group is multiplied
+// (two register buffers), so each thread keeps up to 2 x U x LW bytes in
+// flight.  Activations sit in shared memory as f16 (exact for half, E4M3 and
+// E2M1 inputs), or int8 for i8i8.  Row-lanes are reduced with shuffles inside
+// a warp and in shared memory across warps, in a fixed order; K splits in a
+// cluster (reduce_splits).
+template <int DT, int NR, int LW, int CL, int U>
+__global__ void __launch_bounds__(kThreads, (NR == 1 && DT != kF4F4) ? 4 : 2) gemv_mn_split_kernel(GemvParams p) {
   using Acc = std::conditional_t<DT == kI8I8, int, float>;
   constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights (columns) per thread
   constexpr int CPC = CL * E;                   // columns per CTA
   constexpr int H = E / 2;                      // f16 pairs per thread
   constexpr int RL = kThreads / CL;             // row-lanes
-  constexpr int U = 8;                          // rows in flight per thread
+  constexpr int LPW = LW / 4;                   // 32-bit words per thread per row
   static_assert(DT != kI8I8 || U % 4 == 0, "dp4a takes groups of 4 rows");
+  static_assert(32 % CL == 0 && 32 % U == 0, "lanes and row groups tile a warp and a K chunk");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int kc = p.kchunk;                      // multiple of 32
   unsigned char* xsb = smem_raw;                // [NR][kc] f16 (or int8)
-  Acc* red = reinterpret_cast<Acc*>(smem_raw + (size_t)NR * kc * 2);   // [RL][NR][CPC]
+  Acc* red = reinterpret_cast<Acc*>(smem_raw + (size_t)NR * kc * 2);   // [kWarps][NR][CPC]
+  Acc* tile_sum = red + kWarps * NR * CPC;                             // [NR][CPC]
 
   const int m0 = blockIdx.x * CPC;
   const int kb = blockIdx.y * kc;
   const int ke = min(p.K, kb + kc);
   const int n0 = blockIdx.z * NR;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cl = tid % CL, rl = tid / CL;
 
+  const int mc = m0 + cl * E;   // first column owned by this thread
+  const size_t rb = (size_t)p.M * w_bytes_x2<DT>() / 2;   // bytes per weight row
+  const bool vec = (mc + E <= p.M) && ((size_t)p.M * w_bytes_x2<DT>() % 2 == 0) && (rb % LW == 0);
+  const uint8_t* wcol = reinterpret_cast<const uint8_t*>(p.W) + (size_t)mc * w_bytes_x2<DT>() / 2;
+
+  uint32_t ra[U][LPW], rbuf[U][LPW];
+  auto load = [&](uint32_t (&r)[U][LPW], int g) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = kb + g * U + u;
+      if (k < ke) {
+        const uint8_t* src = wcol + (size_t)k * rb;
+        if constexpr (LW == 16) {
+          const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
+          r[u][0] = v.x; r[u][1] = v.y; r[u][2] = v.z; r[u][3] = v.w;
+        } else if constexpr (LW == 8) {
+          const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
+          r[u][0] = v.x; r[u][1] = v.y;
+        } else {
+          r[u][0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < LPW; ++q) r[u][q] = 0;
+      }
+    }
+  };
+  int g = rl;   // row group: rows kb + g*U .. kb + g*U + U - 1
+  if (vec && kb + g * U < ke) load(ra, g);
+
+  // activations of this K chunk (zero past K and past N)
   for (int i = tid; i < NR * kc; i += kThreads) {
     const int n = i / kc, k = kb + i % kc;
     const bool in = n0 + n < p.N && k < ke;
@@ -223,68 +363,54 @@ __global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
 #pragma unroll
     for (int j = 0; j < E; ++j) acc[n][j] = 0;
 
-  const int mc = m0 + cl * E;   // first column owned by this thread
-  const size_t rb = (size_t)p.M * w_bytes_x2<DT>() / 2;   // bytes per weight row
-  const bool vec = (mc + E <= p.M) && ((size_t)p.M * w_bytes_x2<DT>() % 2 == 0) && (rb % LW == 0);
-  const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.W) + (size_t)mc * w_bytes_x2<DT>() / 2;
+  auto compute = [&](const uint32_t (&r)[U][LPW], int grp) {
+    const int kl = grp * U;
+    if constexpr (DT == kI8I8) {
+      // 4x4 byte transposes, then dp4a over 4 K rows at a time
+#pragma unroll
+      for (int q4 = 0; q4 < U / 4; ++q4) {
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const int x4 = *reinterpret_cast<const int*>(xsb + (size_t)n * kc + kl + 4 * q4);
+#pragma unroll
+          for (int c = 0; c < LPW; ++c) {
+            const uint32_t lo01 = __byte_perm(r[4 * q4][c], r[4 * q4 + 1][c], 0x5140);
+            const uint32_t hi01 = __byte_perm(r[4 * q4][c], r[4 * q4 + 1][c], 0x7362);
+            const uint32_t lo23 = __byte_perm(r[4 * q4 + 2][c], r[4 * q4 + 3][c], 0x5140);
+            const uint32_t hi23 = __byte_perm(r[4 * q4 + 2][c], r[4 * q4 + 3][c], 0x7362);
+            acc[n][4 * c + 0] = __dp4a((int)__byte_perm(lo01, lo23, 0x5410), x4, acc[n][4 * c + 0]);
+            acc[n][4 * c + 1] = __dp4a((int)__byte_perm(lo01, lo23, 0x7632), x4, acc[n][4 * c + 1]);
+            acc[n][4 * c + 2] = __dp4a((int)__byte_perm(hi01, hi23, 0x5410), x4, acc[n][4 * c + 2]);
+            acc[n][4 * c + 3] = __dp4a((int)__byte_perm(hi01, hi23, 0x7632), x4, acc[n][4 * c + 3]);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        uint32_t h[H];
+        widen_chunk<DT, LW>(r[u], h);
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const unsigned short xv = reinterpret_cast<const unsigned short*>(xsb)[(size_t)n * kc + kl + u];
+#pragma unroll
+          for (int j = 0; j < H; ++j) fma2_bcast(acc[n][2 * j], acc[n][2 * j + 1], h[j], xv);
+        }
+      }
+    }
+  };
 
   if (vec) {
-    // rows k = kb + U*rl*... : row-lane rl takes rows kb + U*rl + i (i < U), then jumps by U*RL
-    for (int k0 = kb + U * rl; k0 < ke; k0 += U * RL) {
-      uint32_t raw[U][LW / 4];
-#pragma unroll
-      for (int r = 0; r < U; ++r) {
-        const int k = k0 + r;
-        if (k < ke) {
-          const uint8_t* src = wbase + (size_t)k * rb;
-          if constexpr (LW == 16) {
-            const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
-            raw[r][0] = v.x; raw[r][1] = v.y; raw[r][2] = v.z; raw[r][3] = v.w;
-          } else if constexpr (LW == 8) {
-            const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
-            raw[r][0] = v.x; raw[r][1] = v.y;
-          } else {
-            raw[r][0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < LW / 4; ++q) raw[r][q] = 0;
-        }
-      }
-      const int kl = k0 - kb;
-      if constexpr (DT == kI8I8) {
-        // 4x4 byte transposes, then dp4a over 4 K rows at a time
-#pragma unroll
-        for (int g = 0; g < U / 4; ++g) {
-#pragma unroll
-          for (int n = 0; n < NR; ++n) {
-            const int x4 = *reinterpret_cast<const int*>(xsb + (size_t)n * kc + kl + 4 * g);
-#pragma unroll
-            for (int c = 0; c < LW / 4; ++c) {
-              const uint32_t lo01 = __byte_perm(raw[4 * g][c], raw[4 * g + 1][c], 0x5140);
-              const uint32_t hi01 = __byte_perm(raw[4 * g][c], raw[4 * g + 1][c], 0x7362);
-              const uint32_t lo23 = __byte_perm(raw[4 * g + 2][c], raw[4 * g + 3][c], 0x5140);
-              const uint32_t hi23 = __byte_perm(raw[4 * g + 2][c], raw[4 * g + 3][c], 0x7362);
-              acc[n][4 * c + 0] = __dp4a((int)__byte_perm(lo01, lo23, 0x5410), x4, acc[n][4 * c + 0]);
-              acc[n][4 * c + 1] = __dp4a((int)__byte_perm(lo01, lo23, 0x7632), x4, acc[n][4 * c + 1]);
-              acc[n][4 * c + 2] = __dp4a((int)__byte_perm(hi01, hi23, 0x5410), x4, acc[n][4 * c + 2]);
-              acc[n][4 * c + 3] = __dp4a((int)__byte_perm(hi01, hi23, 0x7632), x4, acc[n][4 * c + 3]);
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < U; ++r) {
-          uint32_t h[H];
-          widen_chunk<DT, LW>(raw[r], h);
-#pragma unroll
-          for (int n = 0; n < NR; ++n) {
-            const unsigned short xv = reinterpret_cast<const unsigned short*>(xsb)[(size_t)n * kc + kl + r];
-#pragma unroll
-            for (int j = 0; j < H; ++j) fma2_bcast(acc[n][2 * j], acc[n][2 * j + 1], h[j], xv);
-          }
-        }
-      }
+    while (kb + g * U < ke) {
+      const int g1 = g + RL;
+      const bool more1 = kb + g1 * U < ke;
+      if (more1) load(rbuf, g1);
+      compute(ra, g);
+      if (!more1) break;
+      const int g2 = g1 + RL;
+      if (kb + g2 * U < ke) load(ra, g2);
+      compute(rbuf, g1);
+      g = g2;
     }
   } else {
     for (int k = kb + rl; k < ke; k += RL) {
@@ -307,50 +433,347 @@ __global__ void __launch_bounds__(kThreads) gemv_mn_kernel(GemvParams p) {
     }
   }
 
-  // row-lane reduction in a fixed order: red[rl][n][col], then column sums
+  // row-lanes of a warp (lanes with equal cl): butterfly, the same order every run
 #pragma unroll
-  for (int n = 0; n < NR; ++n)
+  for (int o = CL; o < 32; o <<= 1)
 #pragma unroll
-    for (int j = 0; j < E; ++j) red[((size_t)rl * NR + n) * CPC + cl * E + j] = acc[n][j];
-  __syncthreads();
-  Acc* out = red;   // the sums overwrite row-lane 0's slice, which thread t reads first
-  for (int i = tid; i < NR * CPC; i += kThreads) {
-    Acc sum = 0;
-    for (int q = 0; q < RL; ++q) sum += red[(size_t)q * NR * CPC + i];
-    out[i] = sum;   // only row-lane 0's entry i is overwritten, after it was read
+    for (int n = 0; n < NR; ++n)
+#pragma unroll
+      for (int j = 0; j < E; ++j) acc[n][j] += __shfl_xor_sync(0xffffffffu, acc[n][j], o);
+  if (lane < CL) {
+#pragma unroll
+    for (int n = 0; n < NR; ++n)
+#pragma unroll
+      for (int j = 0; j < E; ++j) red[((size_t)warp * NR + n) * CPC + cl * E + j] = acc[n][j];
   }
   __syncthreads();
-  finish_tile<Acc>(p, out, n0, NR, m0, CPC);
+  for (int i = tid; i < NR * CPC; i += kThreads) {
+    Acc s = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) s += red[(size_t)w * NR * CPC + i];
+    tile_sum[i] = s;
+  }
+  __syncthreads();
+  reduce_splits<Acc>(p, tile_sum, n0, NR, m0, CPC);
+}
+
+// Stream-K form of the [K,M] kernel: persistent CTAs walk equal runs of
+// (slab, row-group) units with two cursors; the split form above serves the
+// K-split tiles.
+template <int DT, int NR, int LW, int CL, int U, bool STREAM>
+__global__ void __launch_bounds__(kThreads, (NR == 1 && DT != kF4F4) ? 4 : 2) gemv_mn_kernel(GemvParams p) {
+  using Acc = std::conditional_t<DT == kI8I8, int, float>;
+  constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights (columns) per thread
+  constexpr int CPC = CL * E;                   // columns per CTA
+  constexpr int H = E / 2;                      // f16 pairs per thread
+  constexpr int RL = kThreads / CL;             // row-lanes
+  constexpr int LPW = LW / 4;                   // 32-bit words per thread per row
+  constexpr int UR = RL * U;                    // rows per unit (one group per thread)
+  static_assert(DT != kI8I8 || U % 4 == 0, "dp4a takes groups of 4 rows");
+  static_assert(32 % CL == 0 && 32 % U == 0, "lanes and row groups tile a warp and a K chunk");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int kc = p.kchunk;                      // rows of X held (multiple of 32; all of K when streaming)
+  unsigned char* xsb = smem_raw;                // [NR][kc] f16 (or int8)
+  Acc* red = reinterpret_cast<Acc*>(smem_raw + (size_t)NR * kc * 2);   // [kWarps][NR][CPC]
+  Acc* tile_sum = red + kWarps * NR * CPC;                             // [NR][CPC]
+
+  const int n0 = blockIdx.z * NR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cl = tid % CL, rl = tid / CL;
+  const size_t rb = (size_t)p.M * w_bytes_x2<DT>() / 2;   // bytes per weight row
+
+  // this CTA's units: [ubeg, uend); a unit is rows kbase .. kbase + UR of one
+  // column slab.  Two cursors (slab, unit-in-slab) walk them without divisions:
+  // one for the loads, one (a unit behind) for the multiplies.
+  int ubeg, uend, xoff, kend_split = p.K, ups, s_beg, k_beg;
+  if constexpr (STREAM) {
+    cta_range(blockIdx.x, gridDim.x, p.total_units, ubeg, uend);
+    xoff = 0;
+    ups = p.units_per_slab;
+    s_beg = ubeg / ups;
+    k_beg = ubeg - s_beg * ups;
+  } else {
+    xoff = blockIdx.y * kc;
+    kend_split = min(p.K, xoff + kc);
+    ubeg = 0;
+    uend = (kend_split - xoff + UR - 1) / UR;
+    ups = uend + 1;   // one slab: the cursor never wraps
+    s_beg = blockIdx.x;
+    k_beg = 0;
+  }
+  auto advance = [&](int& cs, int& ck) {
+    if (++ck == ups) { ck = 0; ++cs; }
+  };
+  // classic mode: threads whose columns straddle M, or rows whose bytes are not
+  // LW-aligned, take the element-wise path (stream mode is only launched when
+  // every 16-byte chunk is whole)
+  const int mc_fixed = blockIdx.x * CPC + cl * E;
+  const bool vec = STREAM || ((mc_fixed + E <= p.M) && ((size_t)p.M * w_bytes_x2<DT>() % 2 == 0) && (rb % LW == 0));
+
+  uint32_t ra[U][LPW], rbuf[U][LPW];
+  int ls = s_beg, lk = k_beg;   // load cursor
+  const uint8_t* wcol0 = reinterpret_cast<const uint8_t*>(p.W) + (size_t)mc_fixed * w_bytes_x2<DT>() / 2;
+  auto load = [&](uint32_t (&r)[U][LPW]) {
+    const int kbase = xoff + lk * UR;
+    bool ok = true;   // classic mode: vec already says the chunk is whole
+    const uint8_t* wcol = wcol0;
+    if constexpr (STREAM) {
+      const int mc = ls * CPC + cl * E;
+      ok = mc + E <= p.M;
+      wcol = reinterpret_cast<const uint8_t*>(p.W) + (size_t)mc * w_bytes_x2<DT>() / 2;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = kbase + rl * U + u;
+      if (ok && k < kend_split) {
+        const uint8_t* src = wcol + (size_t)k * rb;
+        if constexpr (LW == 16) {
+          const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src));
+          r[u][0] = v.x; r[u][1] = v.y; r[u][2] = v.z; r[u][3] = v.w;
+        } else if constexpr (LW == 8) {
+          const uint2 v = __ldcs(reinterpret_cast<const uint2*>(src));
+          r[u][0] = v.x; r[u][1] = v.y;
+        } else {
+          r[u][0] = __ldcs(reinterpret_cast<const unsigned int*>(src));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < LPW; ++q) r[u][q] = 0;
+      }
+    }
+    advance(ls, lk);
+  };
+  if (vec && ubeg < uend) load(ra);   // the first loads go out before the activations are staged
+
+  // activations (zero past K and past N); when streaming, only the rows of
+  // this CTA's units (a cyclic run of units, all of K if it covers a slab)
+  auto stage_row = [&](int n, int k) {   // k: row of X; stored at k - xoff
+    const bool in = n0 + n < p.N && k < kend_split;
+    const size_t at = (size_t)n * kc + (k - xoff);
+    if constexpr (DT == kI8I8) {
+      reinterpret_cast<int8_t*>(xsb)[at] = in ? reinterpret_cast<const int8_t*>(p.X)[(size_t)(n0 + n) * p.K + k] : 0;
+    } else {
+      reinterpret_cast<__half*>(xsb)[at] = __float2half_rn(in ? load_x<DT>(p.X, p.xscale, n0 + n, k, p.K) : 0.f);
+    }
+  };
+  if constexpr (STREAM) {
+    const int nst = min(uend - ubeg, ups);
+    for (int n = 0; n < NR; ++n)
+      for (int v = tid; v < nst * UR; v += kThreads) {
+        int ku = k_beg + v / UR;
+        if (ku >= ups) ku -= ups;
+        stage_row(n, ku * UR + v % UR);
+      }
+  } else {
+    for (int n = 0; n < NR; ++n)
+      for (int v = tid; v < kc; v += kThreads) stage_row(n, xoff + v);
+  }
+  __syncthreads();
+
+  Acc acc[NR][E];
+  auto zero = [&]() {
+#pragma unroll
+    for (int n = 0; n < NR; ++n)
+#pragma unroll
+      for (int j = 0; j < E; ++j) acc[n][j] = 0;
+  };
+  zero();
+
+  auto compute = [&](const uint32_t (&r)[U][LPW], int ck) {
+    const int kl = ck * UR + rl * U;          // row of X in shared memory
+    if (xoff + kl >= kend_split) return;      // all-zero group; its X rows may lie past the staged chunk
+    if constexpr (DT == kI8I8) {
+      // 4x4 byte transposes, then dp4a over 4 K rows at a time
+#pragma unroll
+      for (int q4 = 0; q4 < U / 4; ++q4) {
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const int x4 = *reinterpret_cast<const int*>(xsb + (size_t)n * kc + kl + 4 * q4);
+#pragma unroll
+          for (int c = 0; c < LPW; ++c) {
+            const uint32_t lo01 = __byte_perm(r[4 * q4][c], r[4 * q4 + 1][c], 0x5140);
+            const uint32_t hi01 = __byte_perm(r[4 * q4][c], r[4 * q4 + 1][c], 0x7362);
+            const uint32_t lo23 = __byte_perm(r[4 * q4 + 2][c], r[4 * q4 + 3][c], 0x5140);
+            const uint32_t hi23 = __byte_perm(r[4 * q4 + 2][c], r[4 * q4 + 3][c], 0x7362);
+            acc[n][4 * c + 0] = __dp4a((int)__byte_perm(lo01, lo23, 0x5410), x4, acc[n][4 * c + 0]);
+            acc[n][4 * c + 1] = __dp4a((int)__byte_perm(lo01, lo23, 0x7632), x4, acc[n][4 * c + 1]);
+            acc[n][4 * c + 2] = __dp4a((int)__byte_perm(hi01, hi23, 0x5410), x4, acc[n][4 * c + 2]);
+            acc[n][4 * c + 3] = __dp4a((int)__byte_perm(hi01, hi23, 0x7632), x4, acc[n][4 * c + 3]);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        uint32_t h[H];
+        widen_chunk<DT, LW>(r[u], h);
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const unsigned short xv = reinterpret_cast<const unsigned short*>(xsb)[(size_t)n * kc + kl + u];
+#pragma unroll
+          for (int j = 0; j < H; ++j) fma2_bcast(acc[n][2 * j], acc[n][2 * j + 1], h[j], xv);
+        }
+      }
+    }
+  };
+
+  // row-lanes of a warp (butterfly over lanes with equal cl), then warps in
+  // shared memory: tile_sum[NR][CPC], in the same order every run
+  auto reduce_tile = [&]() {
+#pragma unroll
+    for (int o = CL; o < 32; o <<= 1)
+#pragma unroll
+      for (int n = 0; n < NR; ++n)
+#pragma unroll
+        for (int j = 0; j < E; ++j) acc[n][j] += __shfl_xor_sync(0xffffffffu, acc[n][j], o);
+    if (lane < CL) {
+#pragma unroll
+      for (int n = 0; n < NR; ++n)
+#pragma unroll
+        for (int j = 0; j < E; ++j) red[((size_t)warp * NR + n) * CPC + cl * E + j] = acc[n][j];
+    }
+    __syncthreads();
+    for (int i = tid; i < NR * CPC; i += kThreads) {
+      Acc s = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) s += red[(size_t)w * NR * CPC + i];
+      tile_sum[i] = s;
+    }
+    __syncthreads();
+  };
+
+  int cs = s_beg, ck = k_beg;   // compute cursor
+  auto step = [&](const uint32_t (&r)[U][LPW]) {
+    if constexpr (STREAM) {
+      if (ck == 0 && cs != s_beg) {   // CTA-uniform: a new slab starts, emit the finished piece
+        reduce_tile();
+        stream_emit<Acc>(p, tile_sum, cs - 1, n0, NR, CPC);
+        zero();
+      }
+    }
+    compute(r, ck);
+    advance(cs, ck);
+  };
+
+  if (vec) {
+    for (int uu = ubeg; uu < uend; uu += 2) {
+      if (uu + 1 < uend) load(rbuf);
+      step(ra);
+      if (uu + 1 >= uend) break;
+      if (uu + 2 < uend) load(ra);
+      step(rbuf);
+    }
+  } else {
+    const int mc = mc_fixed;
+    for (int k = xoff + rl; k < kend_split; k += RL) {
+      const int kl = k - xoff;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        const int m = mc + j;
+        if (m >= p.M) break;
+        if constexpr (DT == kI8I8) {
+          const int wv = reinterpret_cast<const int8_t*>(p.W)[(size_t)k * p.M + m];
+#pragma unroll
+          for (int n = 0; n < NR; ++n) acc[n][j] += (int)reinterpret_cast<const int8_t*>(xsb)[(size_t)n * kc + kl] * wv;
+        } else {
+          const float wv = load_w_mn<DT>(p.W, k, m, p.M);
+#pragma unroll
+          for (int n = 0; n < NR; ++n)
+            acc[n][j] = fmaf(__half2float(reinterpret_cast<const __half*>(xsb)[(size_t)n * kc + kl]), wv, acc[n][j]);
+        }
+      }
+    }
+  }
+
+  reduce_tile();
+  if constexpr (STREAM) {
+    if (ubeg < uend) stream_emit<Acc>(p, tile_sum, (uend - 1) / ups, n0, NR, CPC);
+  } else {
+    reduce_splits<Acc>(p, tile_sum, n0, NR, blockIdx.x * CPC, CPC);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // [M,K] weights (mxfp4 family): E2M1 packed along K, UE8M0 [M, K/32]
 // ---------------------------------------------------------------------------
-// Each 16-byte load is one 32-element block with one W scale (and, for
-// mxfp4/a4 and mxfp4/a8, one X scale per row): the block's dot product of
-// the unscaled f16 values is formed exactly in f32 and then multiplied by
-// 2^(sw-127) * 2^(sx-127).
-template <int DT, int NR>
-__global__ void __launch_bounds__(kThreads) gemv_km_kernel(GemvParams p) {
-  constexpr int RPW = 4;              // output columns per warp
-  constexpr int CPC = kWarps * RPW;   // 32 columns per CTA
+// A warp owns 4 weight rows (output columns); 8 lanes share a row and take
+// its 16-byte blocks (32 E2M1 values, one W scale each) 8 apart, so every
+// load instruction reads 128 contiguous bytes of 4 rows.  U blocks per lane
+// are in flight per buffer, two buffers as in the [K,M] kernel.  Each block's
+// dot product of the unscaled f16 values is formed exactly in f32 and then
+// multiplied by 2^(sw-127) * 2^(sx-127).  The activations sit in shared
+// memory as f16 blocks padded to 80 bytes, so that the 8 lanes of a row read
+// 8 different bank groups.
+template <int DT, int NR, int LPR, int U, bool STREAM>
+__global__ void __launch_bounds__(kThreads, NR == 1 ? 4 : 2) gemv_km_kernel(GemvParams p) {
+  constexpr int RPW = 32 / LPR;       // weight rows (output columns) per warp
+  constexpr int CPC = kWarps * RPW;   // columns per CTA
+  constexpr int XB = 40;              // f16 slots per 32-element block (80 bytes)
+  constexpr int UB = LPR * U;         // blocks of 32 K elements per unit
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int kc = p.kchunk;            // multiple of 32
-  __half* xs = reinterpret_cast<__half*>(smem_raw);                       // [NR][kc] unscaled
-  float* xsc = reinterpret_cast<float*>(smem_raw + (size_t)NR * kc * 2);   // [NR][kc/32]
-  float* red = xsc + NR * (kc / 32);                                       // [NR][CPC]
+  const int kc = p.kchunk;            // K elements of X held (multiple of 32; all of K when streaming)
+  const int kcb = kc / 32;
+  __half* xs = reinterpret_cast<__half*>(smem_raw);                              // [NR][kcb][XB]
+  float* xsc = reinterpret_cast<float*>(smem_raw + (size_t)NR * kcb * XB * 2);  // [NR][kcb]
+  float* tile_sum = xsc + NR * kcb;                                              // [NR][CPC]
 
-  const int m0 = blockIdx.x * CPC;
-  const int kb = blockIdx.y * kc;
-  const int ke = min(p.K, kb + kc);
   const int n0 = blockIdx.z * NR;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kbpr = p.K / 32;
+  const int r = lane / LPR, j = lane % LPR;
+  const int kbpr = p.K / 32;          // blocks per weight row
 
-  for (int i = tid; i < NR * kc; i += kThreads) {
-    const int n = i / kc, k = kb + i % kc;
+  // this CTA's units: [ubeg, uend); a unit is blocks bbase .. bbase + UB of one
+  // group of CPC weight rows, walked by division-free cursors as in the [K,M] kernel
+  int ubeg, uend, xoffb, bend_split = kbpr, ups, s_beg, k_beg;
+  if constexpr (STREAM) {
+    cta_range(blockIdx.x, gridDim.x, p.total_units, ubeg, uend);
+    xoffb = 0;
+    ups = p.units_per_slab;
+    s_beg = ubeg / ups;
+    k_beg = ubeg - s_beg * ups;
+  } else {
+    xoffb = blockIdx.y * kcb;
+    bend_split = min(kbpr, xoffb + kcb);
+    ubeg = 0;
+    uend = (bend_split - xoffb + UB - 1) / UB;
+    ups = uend + 1;
+    s_beg = blockIdx.x;
+    k_beg = 0;
+  }
+  auto advance = [&](int& cs, int& ck) {
+    if (++ck == ups) { ck = 0; ++cs; }
+  };
+
+  uint4 wa[U], wbuf[U];
+  uint32_t sa[U], sbuf[U];
+  int ls = s_beg, lk = k_beg;   // load cursor
+  auto load = [&](uint4 (&w)[U], uint32_t (&sc)[U]) {
+    const int bbase = xoffb + lk * UB;
+    const int m = ls * CPC + warp * RPW + r;
+    const bool mok = m < p.M;
+    const uint8_t* wrow = reinterpret_cast<const uint8_t*>(p.W) + (size_t)(mok ? m : 0) * (p.K / 2);
+    const uint8_t* srow = p.wscale + (size_t)(mok ? m : 0) * kbpr;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int blk = bbase + j + LPR * u;
+      if (mok && blk < bend_split) {
+        w[u] = __ldcs(reinterpret_cast<const uint4*>(wrow + (size_t)blk * 16));
+        sc[u] = __ldg(srow + blk);
+      } else {
+        w[u] = make_uint4(0, 0, 0, 0);
+        sc[u] = 0;
+      }
+    }
+    advance(ls, lk);
+  };
+  if (ubeg < uend) load(wa, sa);   // the first loads go out before the activations are staged
+
+  // activations as unscaled f16 (exact), zero past K and past N; when
+  // streaming, only the blocks of this CTA's units
+  auto stage_x = [&](int n, int kl) {   // kl: element of the staged chunk
+    const int k = xoffb * 32 + kl;
     float v = 0.f;
-    if (n0 + n < p.N && k < ke) {
+    if (n0 + n < p.N && k < bend_split * 32) {
       const size_t xi = (size_t)(n0 + n) * p.K + k;
       if constexpr (x_is_half(DT)) {
         v = dec_f16(reinterpret_cast<const uint16_t*>(p.X)[xi]);
@@ -361,10 +784,23 @@ __global__ void __launch_bounds__(kThreads) gemv_km_kernel(GemvParams p) {
         v = dec_e2m1((xi & 1) ? (byte >> 4) : (byte & 0xF));
       }
     }
-    xs[i] = __float2half_rn(v);   // exact: half, E4M3 and E2M1 values are f16 values
+    xs[((size_t)n * kcb + kl / 32) * XB + kl % 32] = __float2half_rn(v);
+  };
+  if constexpr (STREAM) {
+    constexpr int EU = UB * 32;   // elements per unit
+    const int nst = min(uend - ubeg, ups);
+    for (int n = 0; n < NR; ++n)
+      for (int v = tid; v < nst * EU; v += kThreads) {
+        int ku = k_beg + v / EU;
+        if (ku >= ups) ku -= ups;
+        stage_x(n, ku * EU + v % EU);
+      }
+  } else {
+    for (int n = 0; n < NR; ++n)
+      for (int v = tid; v < kc; v += kThreads) stage_x(n, v);
   }
-  for (int i = tid; i < NR * (kc / 32); i += kThreads) {
-    const int n = i / (kc / 32), blk = kb / 32 + i % (kc / 32);
+  for (int i = tid; i < NR * kcb; i += kThreads) {
+    const int n = i / kcb, blk = xoffb + i % kcb;
     float sc = 1.f;
     if constexpr (x_scaled(DT)) {
       if (n0 + n < p.N && blk < kbpr) sc = dec_ue8m0(p.xscale[(size_t)(n0 + n) * kbpr + blk]);
@@ -373,82 +809,83 @@ __global__ void __launch_bounds__(kThreads) gemv_km_kernel(GemvParams p) {
   }
   __syncthreads();
 
-  float acc[NR][RPW];
+  float acc[NR];
 #pragma unroll
-  for (int n = 0; n < NR; ++n)
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) acc[n][r] = 0.f;
+  for (int n = 0; n < NR; ++n) acc[n] = 0.f;
 
-  const int kblocks = (ke - kb) / 32;  // kchunk and K are multiples of 32
-  const uint8_t* W = reinterpret_cast<const uint8_t*>(p.W);
-  constexpr int BPL = 4;               // blocks per lane in flight, per row
-  for (int b0 = lane; b0 < kblocks; b0 += 32 * BPL) {
-    uint4 wv[BPL][RPW];
-    float sc[BPL][RPW];
+  auto compute = [&](const uint4 (&w)[U], const uint32_t (&sc)[U], int ck) {
+    const int bbase = xoffb + ck * UB;
 #pragma unroll
-    for (int t = 0; t < BPL; ++t) {
-      const int blk = b0 + 32 * t;
+    for (int u = 0; u < U; ++u) {
+      const int blk = bbase + j + LPR * u;
+      if (blk >= bend_split) continue;
+      const int bl = blk - xoffb;     // block index in shared memory
+      uint32_t h[16];
+      const uint32_t words[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        const int m = m0 + warp * RPW + r;
-        if (m < p.M && blk < kblocks) {
-          const int k = kb + blk * 32;
-          wv[t][r] = __ldcs(reinterpret_cast<const uint4*>(W + ((size_t)m * p.K + k) / 2));
-          sc[t][r] = dec_ue8m0(__ldg(p.wscale + (size_t)m * kbpr + k / 32));
-        } else {
-          wv[t][r] = make_uint4(0, 0, 0, 0);
-          sc[t][r] = 0.f;
-        }
+      for (int q = 0; q < 4; ++q) {
+        uint32_t t4[4];
+        e2m1x8_to_h2(words[q], t4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[4 * q + i] = t4[i];
       }
-    }
-#pragma unroll
-    for (int t = 0; t < BPL; ++t) {
-      const int blk = b0 + 32 * t;
-      if (blk >= kblocks) break;
+      const float ws = dec_ue8m0(sc[u]);
 #pragma unroll
       for (int n = 0; n < NR; ++n) {
-        const uint4* xq = reinterpret_cast<const uint4*>(xs + (size_t)n * kc + blk * 32);
-        uint32_t x2[16];
+        const uint4* xq = reinterpret_cast<const uint4*>(xs + ((size_t)n * kcb + bl) * XB);
+        float d = 0.f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 v = xq[q];
-          x2[4 * q] = v.x; x2[4 * q + 1] = v.y; x2[4 * q + 2] = v.z; x2[4 * q + 3] = v.w;
+          const uint4 xv = xq[q];
+          fma2_dot(d, h[4 * q + 0], xv.x);
+          fma2_dot(d, h[4 * q + 1], xv.y);
+          fma2_dot(d, h[4 * q + 2], xv.z);
+          fma2_dot(d, h[4 * q + 3], xv.w);
         }
-        const float xsn = xsc[n * (kc / 32) + blk];
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          float d = 0.f;
-          const uint32_t words[4] = {wv[t][r].x, wv[t][r].y, wv[t][r].z, wv[t][r].w};
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t h[4];
-            e2m1x8_to_h2(words[q], h);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) fma2_dot(d, h[j], x2[4 * q + j]);
-          }
-          acc[n][r] = fmaf(d, sc[t][r] * xsn, acc[n][r]);
-        }
+        acc[n] = fmaf(d, ws * xsc[n * kcb + bl], acc[n]);
       }
     }
-  }
-  // butterfly reduction across lanes (same order on every run)
+  };
+
+  // the lanes of a row (butterfly, same order every run) -> tile_sum[NR][CPC]
+  auto reduce_tile = [&]() {
 #pragma unroll
-  for (int n = 0; n < NR; ++n)
+    for (int n = 0; n < NR; ++n) {
+      float v = acc[n];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      float v = acc[n][r];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[n][r] = v;
+      for (int o = 1; o < LPR; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (j == 0) tile_sum[n * CPC + warp * RPW + r] = v;
+      acc[n] = 0.f;
     }
-  if (lane == 0) {
-#pragma unroll
-    for (int n = 0; n < NR; ++n)
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) red[n * CPC + warp * RPW + r] = acc[n][r];
+    __syncthreads();
+  };
+
+  int cs = s_beg, ck = k_beg;   // compute cursor
+  auto step = [&](const uint4 (&w)[U], const uint32_t (&sc)[U]) {
+    if constexpr (STREAM) {
+      if (ck == 0 && cs != s_beg) {   // CTA-uniform: a new row group starts, emit the finished piece
+        reduce_tile();
+        stream_emit<float>(p, tile_sum, cs - 1, n0, NR, CPC);
+      }
+    }
+    compute(w, sc, ck);
+    advance(cs, ck);
+  };
+
+  for (int uu = ubeg; uu < uend; uu += 2) {
+    if (uu + 1 < uend) load(wbuf, sbuf);
+    step(wa, sa);
+    if (uu + 1 >= uend) break;
+    if (uu + 2 < uend) load(wa, sa);
+    step(wbuf, sbuf);
   }
-  __syncthreads();
-  finish_tile<float>(p, red, n0, NR, m0, CPC);
+
+  reduce_tile();
+  if constexpr (STREAM) {
+    if (ubeg < uend) stream_emit<float>(p, tile_sum, (uend - 1) / ups, n0, NR, CPC);
+  } else {
+    reduce_splits<float>(p, tile_sum, n0, NR, blockIdx.x * CPC, CPC);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -460,10 +897,18 @@ constexpr bool is_kmajor() { return w_is_mx(DT); }
 // Rows per CTA: 1, 2, 4 or 8 (larger N uses several row blocks).
 inline int pick_nr(int N) { return N <= 1 ? 1 : N <= 2 ? 2 : N <= 4 ? 4 : 8; }
 
-// Lanes side by side on one weight row ([K,M] kernel): a narrow slab gives
-// enough CTAs without splitting K; wide slabs for many rows (N > 1 runs are
-// compute-heavier and prefer fewer, wider CTAs).
-constexpr int kLanesPerRow = 4;
+// [K,M] kernel: 16-byte lanes side by side on one weight row (CL x 16 = 128
+// contiguous bytes per row and CTA) and rows per group.
+constexpr int kLanesPerRow = 8;
+constexpr int kRowsPerGroup = 4;
+// [M,K] kernel: lanes per weight row, 16-byte blocks per lane and buffer.
+constexpr int kLanesPerMxRow = 8;
+constexpr int kBlocksPerLane = 4;
+// K splits reduced inside a thread-block cluster (portable cluster size).
+constexpr int kMaxClusterSplit = 8;
+constexpr size_t kMaxGemvSmem = 227 * 1024;
+// stream-K: grid bound (persistent CTAs) and the partial-slot layout sized by it
+constexpr int kMaxStreamCtas = 1024;
 
 // Bytes loaded per thread per weight row, so that NR * E <= 64 accumulators.
 template <int DT>
@@ -475,7 +920,7 @@ constexpr int pick_lw(int NR) {
 }
 
 int cols_per_cta(int dt, int N) {
-  if (dt == kMXFP4 || dt == kMX4X4 || dt == kMX8X4 || dt == kF8X4) return 32;
+  if (w_is_mx(dt)) return kWarps * (32 / kLanesPerMxRow);
   const int nr = pick_nr(N);
   const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
   int lw = 16;
@@ -494,34 +939,104 @@ int kchunk_for(int K, int ksplit) {
   return (kc + 31) / 32 * 32;
 }
 
+size_t gemv_smem(int dt, int N, int kc) {
+  const size_t nr = (size_t)pick_nr(N);
+  if (w_is_mx(dt)) return nr * (kc / 32) * 80 + nr * (kc / 32) * 4 + nr * cols_per_cta(dt, N) * 4;
+  return nr * kc * 2 + (size_t)(kWarps + 1) * nr * cols_per_cta(dt, N) * 4;
+}
+
+template <typename KernelT>
+cudaError_t launch_k(KernelT k, const GemvParams& p, dim3 grid, size_t smem, int num_sms, cudaStream_t st) {
+  if (smem > kMaxGemvSmem) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  if (p.stream) {
+    // persistent: as many CTAs as fit on the GPU at once, never more than units
+    int per_sm = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    long g = (long)(per_sm > 0 ? per_sm : 1) * (num_sms > 0 ? num_sms : 148);
+    if (g > kMaxStreamCtas) g = kMaxStreamCtas;
+    if (g > p.total_units) g = p.total_units;
+    grid.x = (unsigned)g;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.cluster ? (unsigned)p.ksplit : 1u;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, p);
+}
+
 template <int DT, int NR>
-cudaError_t launch_nr(const GemvParams& p, dim3 grid, cudaStream_t st) {
-  size_t smem;
+cudaError_t launch_nr(const GemvParams& p, dim3 grid, int num_sms, cudaStream_t st) {
+  const size_t smem = gemv_smem(DT, p.N, p.kchunk);
   if constexpr (is_kmajor<DT>()) {
-    smem = (size_t)NR * p.kchunk * 2 + (size_t)NR * (p.kchunk / 32) * 4 + (size_t)NR * 32 * 4;
-    auto k = gemv_km_kernel<DT, NR>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, kThreads, smem, st>>>(p);
+    if (p.stream)
+      return launch_k(gemv_km_kernel<DT, NR, kLanesPerMxRow, kBlocksPerLane, true>, p, grid, smem, num_sms, st);
+    return launch_k(gemv_km_kernel<DT, NR, kLanesPerMxRow, kBlocksPerLane, false>, p, grid, smem, num_sms, st);
   } else {
     constexpr int LW = pick_lw<DT>(NR);
-    constexpr int E = LW * 2 / w_bytes_x2<DT>();
-    constexpr int CL = kLanesPerRow;
-    smem = (size_t)NR * p.kchunk * 2 + (size_t)(kThreads / CL) * NR * CL * E * 4;
-    auto k = gemv_mn_kernel<DT, NR, LW, CL>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    k<<<grid, kThreads, smem, st>>>(p);
+    if (p.stream)
+      return launch_k(gemv_mn_kernel<DT, NR, LW, kLanesPerRow, kRowsPerGroup, true>, p, grid, smem, num_sms, st);
+    return launch_k(gemv_mn_split_kernel<DT, NR, LW, kLanesPerRow, kRowsPerGroup>, p, grid, smem, num_sms, st);
   }
-  return cudaGetLastError();
 }
 
 template <int DT>
-cudaError_t launch_dt(const GemvParams& p, dim3 grid, int nr, cudaStream_t st) {
+cudaError_t launch_dt(const GemvParams& p, dim3 grid, int nr, int num_sms, cudaStream_t st) {
   switch (nr) {
-    case 1: return launch_nr<DT, 1>(p, grid, st);
-    case 2: return launch_nr<DT, 2>(p, grid, st);
-    case 4: return launch_nr<DT, 4>(p, grid, st);
-    default: return launch_nr<DT, 8>(p, grid, st);
+    case 1: return launch_nr<DT, 1>(p, grid, num_sms, st);
+    case 2: return launch_nr<DT, 2>(p, grid, num_sms, st);
+    case 4: return launch_nr<DT, 4>(p, grid, num_sms, st);
+    default: return launch_nr<DT, 8>(p, grid, num_sms, st);
   }
+}
+
+cudaError_t launch_any(int dt, const GemvParams& p, dim3 grid, int nr, int num_sms, cudaStream_t st) {
+  switch (dt) {
+    case kFP16: return launch_dt<kFP16>(p, grid, nr, num_sms, st);
+    case kINT8: return launch_dt<kINT8>(p, grid, nr, num_sms, st);
+    case kI8I8: return launch_dt<kI8I8>(p, grid, nr, num_sms, st);
+    case kFP8: return launch_dt<kFP8>(p, grid, nr, num_sms, st);
+    case kF8F8: return launch_dt<kF8F8>(p, grid, nr, num_sms, st);
+    case kF4F4: return launch_dt<kF4F4>(p, grid, nr, num_sms, st);
+    case kMXFP4: return launch_dt<kMXFP4>(p, grid, nr, num_sms, st);
+    case kMX4X4: return launch_dt<kMX4X4>(p, grid, nr, num_sms, st);
+    case kMX8X4: return launch_dt<kMX8X4>(p, grid, nr, num_sms, st);
+    case kF8X4: return launch_dt<kF8X4>(p, grid, nr, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ---- stream-K geometry ---------------------------------------------------------
+struct StreamGeom {
+  int nslabs, ups, units, kp, nrowblk, cpc;
+  size_t smem;
+};
+
+StreamGeom stream_geom(int dt, int N, int K, int M) {
+  StreamGeom g;
+  const int nr = pick_nr(N);
+  g.cpc = cols_per_cta(dt, N);
+  g.nslabs = (M + g.cpc - 1) / g.cpc;
+  // K elements per unit: one row group per thread ([K,M]) or U blocks per lane ([M,K])
+  const int kpu = w_is_mx(dt) ? kLanesPerMxRow * kBlocksPerLane * 32 : (kThreads / kLanesPerRow) * kRowsPerGroup;
+  g.ups = (K + kpu - 1) / kpu;
+  g.kp = g.ups * kpu;
+  g.units = g.nslabs * g.ups;
+  g.nrowblk = (N + nr - 1) / nr;
+  g.smem = gemv_smem(dt, N, g.kp);
+  return g;
 }
 
 }  // namespace
@@ -541,23 +1056,37 @@ cudaError_t launch_l2_flush(const void* buf, size_t bytes, int num_sms, cudaStre
   return cudaGetLastError();
 }
 
+// Effective number of K splits for a requested one (chunks are whole 32s).
+static int eff_splits(int K, int ksplit) {
+  const int kc = kchunk_for(K, ksplit < 1 ? 1 : ksplit);
+  return (K + kc - 1) / kc;
+}
+
+bool gemv_supported(int dt, int ksplit, int N, int K, int M) {
+  (void)M;
+  if (N < 1 || K < 1 || M < 1) return false;
+  return gemv_smem(dt, N, kchunk_for(K, ksplit < 1 ? 1 : ksplit)) <= kMaxGemvSmem;
+}
+
 int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {
   const int nr = pick_nr(N);
   const long ctas = (long)((M + cols_per_cta(dt, N) - 1) / cols_per_cta(dt, N)) *
                     ((N + nr - 1) / nr);
-  const long target = 4L * (num_sms > 0 ? num_sms : 148);
+  // about two CTAs per SM: measured best on the thin row for every dtype
+  const long target = 2L * (num_sms > 0 ? num_sms : 148);
   int s = 1;
-  if (ctas > kMaxCounterTiles) return 1;
-  while (s < 64 && ctas * s < target && K / (2 * s) >= 64) s *= 2;
+  if (ctas > kMaxCounterTiles) {
+    while (s < 8 && !gemv_supported(dt, s, N, K, M)) s *= 2;   // cluster splits need no counters
+    return s;
+  }
+  while (s < 64 && ((ctas * s < target && K / (2 * s) >= 64) || !gemv_supported(dt, s, N, K, M))) s *= 2;
   return s;
 }
 
 size_t gemv_workspace(int dt, int ksplit, int N, int K, int M) {
   (void)dt;
-  if (ksplit <= 1) return 0;
-  const int kc = kchunk_for(K, ksplit);
-  const int eff = (K + kc - 1) / kc;
-  if (eff <= 1) return 0;
+  const int eff = eff_splits(K, ksplit);
+  if (eff <= kMaxClusterSplit) return 0;   // one CTA, or a cluster reducing in shared memory
   return kCounterBytes + (size_t)eff * N * M * 4;
 }
 
@@ -574,32 +1103,71 @@ cudaError_t launch_gemv(const RunArgs& a, int ksplit) {
   p.M = a.M;
   p.kchunk = kchunk_for(a.K, ksplit);
   p.ksplit = (a.K + p.kchunk - 1) / p.kchunk;
+  p.cluster = p.ksplit > 1 && p.ksplit <= kMaxClusterSplit;
   const int nr = pick_nr(a.N);
   const int cpc = cols_per_cta(a.dt, a.N);
   dim3 grid((a.M + cpc - 1) / cpc, p.ksplit, (a.N + nr - 1) / nr);
-  if (p.ksplit > 1) {
+  p.part = nullptr;
+  p.counters = nullptr;
+  if (p.ksplit > kMaxClusterSplit) {
     if ((size_t)grid.x * grid.z > (size_t)kMaxCounterTiles) return cudaErrorInvalidValue;
     if (a.ws == nullptr || a.ws_bytes < gemv_workspace(a.dt, ksplit, a.N, a.K, a.M))
       return cudaErrorInvalidValue;
     p.counters = reinterpret_cast<unsigned*>(a.ws);
     p.part = reinterpret_cast<char*>(a.ws) + kCounterBytes;
-  } else {
-    p.part = nullptr;
-    p.counters = nullptr;
   }
-  switch (a.dt) {
-    case kFP16: return launch_dt<kFP16>(p, grid, nr, a.stream);
-    case kINT8: return launch_dt<kINT8>(p, grid, nr, a.stream);
-    case kI8I8: return launch_dt<kI8I8>(p, grid, nr, a.stream);
-    case kFP8: return launch_dt<kFP8>(p, grid, nr, a.stream);
-    case kF8F8: return launch_dt<kF8F8>(p, grid, nr, a.stream);
-    case kF4F4: return launch_dt<kF4F4>(p, grid, nr, a.stream);
-    case kMXFP4: return launch_dt<kMXFP4>(p, grid, nr, a.stream);
-    case kMX4X4: return launch_dt<kMX4X4>(p, grid, nr, a.stream);
-    case kMX8X4: return launch_dt<kMX8X4>(p, grid, nr, a.stream);
-    case kF8X4: return launch_dt<kF8X4>(p, grid, nr, a.stream);
-    default: return cudaErrorInvalidValue;
+  p.stream = 0;
+  p.nslabs = p.units_per_slab = p.total_units = 0;
+  return launch_any(a.dt, p, grid, nr, a.num_sms, a.stream);
+}
+
+// ---- stream-K thin-row tile ("stream") --------------------------------------------
+bool stream_supported(int dt, int N, int K, int M) {
+  if (N < 1 || N > 16 || K < 1 || M < 1) return false;
+  if (!w_is_mx(dt)) {
+    // every thread's 16/8/4-byte chunk is whole and aligned on every row
+    const int nr = pick_nr(N);
+    const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
+    int lw = 16;
+    while (lw > 4 && nr * (lw * 2 / bx2) > 64) lw /= 2;
+    const int e = lw * 2 / bx2;
+    if (((long)M * bx2) % 2 != 0 || M % e != 0) return false;
+    if (((long)M * bx2 / 2) % lw != 0) return false;
   }
+  const StreamGeom g = stream_geom(dt, N, K, M);
+  if ((size_t)g.nrowblk * g.nslabs * sizeof(unsigned) > kCounterBytes) return false;
+  return g.smem <= kMaxGemvSmem;
+}
+
+size_t stream_workspace(int dt, int N, int K, int M) {
+  const StreamGeom g = stream_geom(dt, N, K, M);
+  const size_t slots = (size_t)g.nrowblk * (g.nslabs + kMaxStreamCtas);
+  return kCounterBytes + slots * pick_nr(N) * g.cpc * 4;
+}
+
+cudaError_t launch_stream(const RunArgs& a) {
+  if (!stream_supported(a.dt, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+  if (!a.ws || a.ws_bytes < stream_workspace(a.dt, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+  const StreamGeom g = stream_geom(a.dt, a.N, a.K, a.M);
+  GemvParams p;
+  p.X = a.X;
+  p.W = a.W;
+  p.Y = a.Y;
+  p.xscale = a.xscale;
+  p.wscale = a.wscale;
+  p.N = a.N;
+  p.K = a.K;
+  p.M = a.M;
+  p.ksplit = 1;
+  p.kchunk = g.kp;
+  p.cluster = 0;
+  p.counters = reinterpret_cast<unsigned*>(a.ws);
+  p.part = reinterpret_cast<char*>(a.ws) + kCounterBytes;
+  p.stream = 1;
+  p.nslabs = g.nslabs;
+  p.units_per_slab = g.ups;
+  p.total_units = g.units;
+  return launch_any(a.dt, p, dim3(1, 1, g.nrowblk), pick_nr(a.N), a.num_sms, a.stream);
 }
 
 }  // namespace mlpg

@@ -23,6 +23,9 @@ struct RunArgs {
 };
 
 // ---- CUDA-core split-K GEMV (thin rows; also the any-shape fallback) --------
+// Up to 8 K splits reduce inside a thread-block cluster (no workspace); more
+// splits reduce through the workspace.
+bool gemv_supported(int dt, int ksplit, int N, int K, int M);
 int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms);
 size_t gemv_workspace(int dt, int ksplit, int N, int K, int M);
 cudaError_t launch_gemv(const RunArgs& a, int ksplit);

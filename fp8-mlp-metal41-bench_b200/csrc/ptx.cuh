@@ -91,6 +91,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// mbar_wait for a whole warp: lane 0 polls (bounded), the other lanes wait
+// at the shuffle instead of spinning; once the phase has completed every lane
+// takes its own (immediately successful) try_wait for acquire ordering.  Valid
+// when the barrier cannot complete a further phase before this warp arrives
+// somewhere (a ring whose slot this warp has yet to release).  Call converged.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const AbortCtl& c,
+                                               int where) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, c, where) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_try_wait(smem_u32(bar), parity);
+  return ok != 0;
+}
+
 // ---- TMA -------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -246,6 +260,13 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
+}
+
+// 32-bit load from distributed shared memory (an address from mapa_shared).
+__device__ __forceinline__ uint32_t ld_dsmem_u32(uint32_t cluster_addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.b32 %0, [%1];" : "=r"(v) : "r"(cluster_addr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
