@@ -140,19 +140,23 @@ struct Cfg {
   static constexpr uint32_t B_LBO = T::b_mn ? (uint32_t)B_BOX_BYTES : 16u;
   static constexpr uint32_t B_ADV = T::b_mn ? (uint32_t)(MMA_K_BYTES * 8 / T::b_bits) * kRowBytes
                                             : (uint32_t)MMA_K_BYTES;
-  // scale factors: per stage and MMA one 512-byte block for A, BN/128 for B
+  // scale factors: one 32-bit TMEM cell per row holds 4 UE8M0 bytes, which
+  // serve 4 MMAs of kind::mxf8f6f4 (one block of 32 each) or 2 of kind::mxf4
+  // (two blocks each); the MMA picks its byte with the descriptor's scale-factor
+  // id.  Per stage: SF_CELLS 512-byte blocks for A, BN/128 times that for B.
   static constexpr int SF_B_CHUNKS = BN / 128;
-  static constexpr int SF_A_BYTES = SCALED ? MMAS_PER_STAGE * kSfChunk : 0;
-  static constexpr int SF_B_BYTES = SCALED ? MMAS_PER_STAGE * SF_B_CHUNKS * kSfChunk : 0;
+  static constexpr int SF_CELLS = SCALED ? MMAS_PER_STAGE * T::nsf / 4 : 0;
+  static constexpr int SF_A_BYTES = SF_CELLS * kSfChunk;
+  static constexpr int SF_B_BYTES = SF_CELLS * SF_B_CHUNKS * kSfChunk;
   static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
-  // TMEM: [0, 2*BN) accumulators; then per stage 4 columns per MMA for A and
-  // 4*BN/128 per MMA for B (one 32-bit column per 32 rows, byte s = block s)
+  // TMEM: [0, 2*BN) accumulators; then per stage and cell 4 columns for A and
+  // 4*BN/128 for B (one 32-bit column per 32 rows, byte s = block s)
   static constexpr int ACC_COLS = BN;
   static constexpr int SF_COL0 = 2 * BN;
   static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
-  static constexpr int SF_COLS_STAGE = SCALED ? MMAS_PER_STAGE * (SF_COLS_A + SF_COLS_B) : 0;
+  static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
   static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN + STAGES * SF_COLS_STAGE);
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
@@ -183,13 +187,14 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int&
 }
 
 // Scale-factor packing pre-pass.  For every 128-row tile t of an operand,
-// every K stage st and every MMA kk of the stage, one 512-byte block:
-// byte (16*r0 + 4*j + s) = UE8M0 scale of row 128*t + r0 + 32*j for k-block
-// st*nb + kk*nsf + s (s < nsf; 127 = 1.0 outside the matrix).  That is the
-// source layout of tcgen05.cp.32x128b.warpx4: row r0's 16 bytes land in TMEM
-// lane r0 of every lane quadrant, 32-bit column j, where the block-scaled
-// MMA reads the scale of row r0 + 32*j.  The producer then fetches each
-// stage's blocks with one 1-D bulk copy per operand.
+// every K stage st and every cell g of the stage (4 k-blocks), one 512-byte
+// block: byte (16*r0 + 4*j + s) = UE8M0 scale of row 128*t + r0 + 32*j for
+// k-block st*nb + 4*g + s (127 = 1.0 outside the matrix).  That is the source
+// layout of tcgen05.cp.32x128b.warpx4: row r0's 16 bytes land in TMEM lane r0
+// of every lane quadrant, 32-bit column j, where the block-scaled MMA reads the
+// scales of row r0 + 32*j, byte s selected by the descriptor's scale-factor id.
+// The producer then fetches each stage's blocks with one 1-D bulk copy per
+// operand.
 struct SfPackJob {
   const uint8_t* plane;   // [rows, kbpr]
   uint8_t* out;           // [tiles][stages][4][512]
@@ -197,13 +202,13 @@ struct SfPackJob {
 };
 
 __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb, int kbpr, int stages, int nb,
-                                                      int nsf) {
+                                                      int cells) {
   const SfPackJob& j = blockIdx.y == 0 ? ja : jb;        // y = 0: X plane, 1: W plane
   if (j.plane == nullptr) return;
-  const int tid = blockIdx.x * 256 + threadIdx.x;       // one thread per (t, st, kk, r0)
+  const int tid = blockIdx.x * 256 + threadIdx.x;       // one thread per (t, st, g, r0)
   const int r0 = tid & 31;
-  const int kk = (tid >> 5) & 3;
-  const int rest = tid >> 7;
+  const int g = (tid >> 5) % cells;
+  const int rest = (tid >> 5) / cells;
   const int st = rest % stages, t = rest / stages;
   if (t >= j.tiles) return;
   const uint8_t* plane = j.plane;
@@ -214,14 +219,14 @@ __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb
   for (int j = 0; j < 4; ++j) {
     const int row = t * 128 + r0 + 32 * j;
     uint32_t v = 0;
-    for (int q = 0; q < nsf; ++q) {
-      const int kblk = st * nb + kk * nsf + q;
+    for (int q = 0; q < 4; ++q) {
+      const int kblk = st * nb + 4 * g + q;
       const uint32_t sc = (row < rows && kblk < kbpr) ? plane[(size_t)row * kbpr + kblk] : 127u;
       v |= sc << (8 * q);
     }
     w[j] = v;
   }
-  *reinterpret_cast<uint4*>(out + ((size_t)((t * stages + st) * 4 + kk)) * 512 + r0 * 16) =
+  *reinterpret_cast<uint4*>(out + ((size_t)((t * stages + st) * cells + g)) * 512 + r0 * 16) =
       make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -349,18 +354,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
           const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
-          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
-            const uint32_t sfa_t = sf_tmem + kk * (C::SF_COLS_A + C::SF_COLS_B);
-            const uint32_t sfb_t = sfa_t + C::SF_COLS_A;
-            tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + kk * kSfChunk : sf_const, 0, 128));
+          for (int g = 0; g < C::SF_CELLS; ++g) {
+            const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+            tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + g * kSfChunk : sf_const, 0, 128));
 #pragma unroll
             for (int c = 0; c < C::SF_B_CHUNKS; ++c)
-              tc_cp_32x128b_warpx4(sfb_t + 4 * c,
-                                   sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::MMAS_PER_STAGE + kk) * kSfChunk
+              tc_cp_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
+                                   sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
                                                      : sf_const, 0, 128));
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            constexpr int per_cell = 4 / T::nsf;   // MMAs served by one cell
+            const int g = kk / per_cell;
+            const uint32_t sfid = (uint32_t)((kk % per_cell) * T::nsf);   // first byte of this MMA's blocks
+            const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+            const uint32_t sfb_t = sfa_t + C::SF_COLS_A;
+            const uint32_t idesc = C::IDESC | (sfid << 4) | (sfid << 29);   // B and A scale-factor ids
             const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
             const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
-            tc_mma_bs<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u, sfa_t, sfb_t);
+            tc_mma_bs<T::kind>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u, sfa_t, sfb_t);
           }
         } else {
 #pragma unroll
@@ -1312,7 +1325,7 @@ size_t round256(size_t x) { return (x + 255) / 256 * 256; }
 // [f4f4: W transposed to [M,K]].
 struct ScaledWs {
   size_t a_bytes = 0, b_bytes = 0, wt_bytes = 0;
-  int stages = 0, a_tiles = 0, b_tiles = 0, nb = 0, nsf = 0;
+  int stages = 0, a_tiles = 0, b_tiles = 0, nb = 0, cells = 0;
   size_t total() const { return round256(a_bytes) + round256(b_bytes) + round256(wt_bytes); }
 };
 
@@ -1321,13 +1334,13 @@ ScaledWs scaled_ws(int dt, int bn, int N, int K, int M) {
   const bool mxf4 = (dt == kMX4X4 || dt == kF4F4);
   const int kps = mxf4 ? 256 : 128;
   w.nb = kps / 32;
-  w.nsf = mxf4 ? 2 : 1;
+  w.cells = w.nb / 4;   // 32-bit cells of 4 k-blocks per stage
   w.stages = (K + kps - 1) / kps;
   w.a_tiles = (N + 127) / 128;
   w.b_tiles = (M + bn - 1) / bn * (bn / 128);
   const bool xp = (dt == kMX4X4 || dt == kMX8X4), wp = (dt != kF4F4);
-  if (xp) w.a_bytes = (size_t)w.a_tiles * w.stages * 4 * kSfChunk;
-  if (wp) w.b_bytes = (size_t)w.b_tiles * w.stages * 4 * kSfChunk;
+  if (xp) w.a_bytes = (size_t)w.a_tiles * w.stages * w.cells * kSfChunk;
+  if (wp) w.b_bytes = (size_t)w.b_tiles * w.stages * w.cells * kSfChunk;
   if (dt == kF4F4) w.wt_bytes = (size_t)M * K / 2;
   return w;
 }
@@ -1347,8 +1360,8 @@ cudaError_t launch_scaled(const RunArgs& a) {
     SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles};
     SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles};
     const int tiles = w.a_tiles > w.b_tiles ? w.a_tiles : w.b_tiles;
-    const int threads = tiles * w.stages * 128;
-    sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.nsf);
+    const int threads = tiles * w.stages * w.cells * 32;
+    sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.cells);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   const void* W = a.W;
