@@ -62,6 +62,11 @@ constexpr int kSfChunk = 512;    // one 32 x 16-byte scale-factor block (one tcg
 template <int DT>
 struct Traits;
 
+// f4f4 on CTA pairs: kind::f8f6f4 with E2M1 x E2M1 (no scales), both
+// operands K-major (W transposed to [M,K] first) and unpacked by TMA into
+// 8-bit containers in shared memory (16U4_ALIGN16B).
+constexpr int kF4F4Pair = 64;
+
 template <>
 struct Traits<kFP16> {
   static constexpr int kind = kKindF16, a_bits = 16, b_bits = 16, nsf = 0;
@@ -97,6 +102,12 @@ struct Traits<kMX8X4> {
   static constexpr int kind = kKindMxF8F6F4, a_bits = 8, b_bits = 8, nsf = 1;
   static constexpr bool b_mn = false, x_plane = true, w_plane = true, b_unpack4 = true;
   static constexpr uint32_t a_fmt = 0, b_fmt = 5, c_fmt = 1;  // E4M3, E2M1
+};
+template <>
+struct Traits<kF4F4Pair> {
+  static constexpr int kind = kKindF8F6F4, a_bits = 8, b_bits = 8, nsf = 0;
+  static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = true;
+  static constexpr uint32_t a_fmt = 5, b_fmt = 5, c_fmt = 1;  // E2M1, E2M1 -> F32
 };
 template <>
 struct Traits<kF8X4> {
@@ -515,6 +526,9 @@ struct Cfg2 {
   static constexpr int A_BYTES = kBM * kRowBytes;
   static constexpr int B_BYTES = BH * kRowBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // transaction bytes: the 16U4_ALIGN16B loads count the packed 4-bit source
+  static constexpr bool UNPACK4 = DT == kF4F4Pair;
+  static constexpr int STAGE_TX = UNPACK4 ? STAGE_BYTES / 2 : STAGE_BYTES;
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;
   static constexpr int MMA_K_BYTES = 32;
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;
@@ -590,8 +604,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Only the leader arrives, expecting both CTAs' bytes; the peer's loads
         // just complete their transactions on the leader's barrier (a remote
         // arrive per stage would put a cross-SM round trip in the peer's loop).
-        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * C::STAGE_BYTES);
-        tma_load_2d_pair(a_dst, &tmA, lfull, kb * (T::a_bits == 16 ? C::K_PER_STAGE : kRowBytes),
+        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * C::STAGE_TX);
+        // x counts elements of the map: 16-bit or 4-bit (unpacking maps) elements, else bytes
+        tma_load_2d_pair(a_dst, &tmA, lfull,
+                         kb * ((T::a_bits == 16 || C::UNPACK4) ? C::K_PER_STAGE : kRowBytes),
                          tm * 256 + (int)rank * kBM);
         if constexpr (T::b_mn) {
 #pragma unroll
@@ -599,7 +615,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(b_dst + j * C::B_BOX_BYTES, &tmB, lfull, tn * BN + (int)rank * C::BH + j * C::B_BOX_MN,
                              kb * C::K_PER_STAGE);
         } else {
-          tma_load_2d_pair(b_dst, &tmB, lfull, kb * kRowBytes, tn * BN + (int)rank * C::BH);
+          tma_load_2d_pair(b_dst, &tmB, lfull, kb * (C::UNPACK4 ? C::K_PER_STAGE : kRowBytes),
+                           tn * BN + (int)rank * C::BH);
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
@@ -1176,13 +1193,20 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
 }
 
 template <int DT, int BN, int STAGES>
-cudaError_t launch_pair(const RunArgs& a) {
+cudaError_t launch_pair(const RunArgs& a, const void* W) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
   CUtensorMap tmA, tmB;
   const CUtensorMapDataType ty8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok;
-  if constexpr (T::a_bits == 16) {
+  if constexpr (C::UNPACK4) {
+    // packed E2M1 rows of K/2 bytes, unpacked to one byte per element in shared memory
+    ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.N,
+                  (uint64_t)a.K / 2, C::K_PER_STAGE, kBM) &&
+         make_map(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.M,
+                  (uint64_t)a.K / 2, C::K_PER_STAGE, C::BH);
+    if (!ok) return cudaErrorInvalidValue;
+  } else if constexpr (T::a_bits == 16) {
     ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K * 2,
                   C::K_PER_STAGE, kBM);
   } else {
@@ -1190,13 +1214,15 @@ cudaError_t launch_pair(const RunArgs& a) {
     ok = make_map(&tmA, a.X, ty8, row_bytes, (uint64_t)a.N, row_bytes, kRowBytes, kBM);
   }
   if (!ok) return cudaErrorInvalidValue;
-  if constexpr (T::b_mn) {
+  if constexpr (C::UNPACK4) {
+    // tmB made above
+  } else if constexpr (T::b_mn) {
     const int es = T::b_bits / 8;
-    ok = make_map(&tmB, a.W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, (uint64_t)a.M, (uint64_t)a.K,
+    ok = make_map(&tmB, W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, (uint64_t)a.M, (uint64_t)a.K,
                   (uint64_t)a.M * es, C::B_BOX_MN, C::K_PER_STAGE);
   } else {
     const uint64_t row_bytes = (uint64_t)a.K * T::b_bits / 8;
-    ok = make_map(&tmB, a.W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH);
+    ok = make_map(&tmB, W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH);
   }
   if (!ok) return cudaErrorInvalidValue;
   TcParams p;
@@ -1299,6 +1325,7 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
     if (bn != 256) return false;
     if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
     if (dt == kI8I8 || dt == kF8F8) return K % 16 == 0 && M % 16 == 0;
+    if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;   // kind::f8f6f4 on unpacked E2M1
     return false;
   }
   if (bm != 128) return false;
@@ -1374,6 +1401,19 @@ cudaError_t launch_scaled(const RunArgs& a) {
   return launch_cfg<DT, BN, STAGES>(a, W, pa, pb);
 }
 
+// f4f4 on CTA pairs: transpose W to [M,K] into the workspace, then
+// kind::f8f6f4 (E2M1 x E2M1) over both operands unpacked by TMA.
+cudaError_t launch_f4f4_pair(const RunArgs& a) {
+  const ScaledWs w = scaled_ws(kF4F4, 256, a.N, a.K, a.M);
+  if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
+  uint8_t* wt = static_cast<uint8_t*>(a.ws) + round256(w.a_bytes) + round256(w.b_bytes);
+  dim3 grid((a.M + kTrM - 1) / kTrM, (a.K + kTrK - 1) / kTrK);
+  transpose_fp4_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), wt, a.K, a.M);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_pair<kF4F4Pair, 256, 6>(a, wt);
+}
+
 }  // namespace
 
 size_t tc_workspace(int dt, int bn, int N, int K, int M) {
@@ -1392,9 +1432,10 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
   if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
   if (bm == 256) {
     switch (a.dt) {
-      case kFP16: return launch_pair<kFP16, 256, 6>(a);
-      case kI8I8: return launch_pair<kI8I8, 256, 6>(a);
-      case kF8F8: return launch_pair<kF8F8, 256, 6>(a);
+      case kFP16: return launch_pair<kFP16, 256, 6>(a, a.W);
+      case kI8I8: return launch_pair<kI8I8, 256, 6>(a, a.W);
+      case kF8F8: return launch_pair<kF8F8, 256, 6>(a, a.W);
+      case kF4F4: return launch_f4f4_pair(a);
       default: return cudaErrorInvalidValue;
     }
   }
