@@ -41,7 +41,7 @@ class ShapeCase:
 SUITE = [ShapeCase("square", 4096, 4096, 4096, 100), ShapeCase("thin", 1, 4096, 11008, 200),
          ShapeCase("fat", 2048, 4096, 11008, 50)]
 
-BOOL_FLAGS = ("--suite", "--autotune", "--no-profile", "--allgather", "--flush")
+BOOL_FLAGS = ("--suite", "--autotune", "--no-profile", "--allgather", "--flush", "--peak")
 
 
 @dataclass
@@ -63,6 +63,7 @@ class Args:
     seed: int = 0
     rotate: int = 1
     flush: bool = False
+    peak: bool = False      # tensor-core peak probe instead of the GEMM (tune/peak.swift)
 
 
 class BenchExit(Exception):
@@ -95,6 +96,8 @@ def parse_args(argv, tiles=None) -> Args:
                 a.allgather = True
             elif key == "--flush":
                 a.flush = True
+            elif key == "--peak":
+                a.peak = True
             i += 1
             continue
         i += 1
@@ -410,12 +413,39 @@ def main(argv=None) -> int:
         return 2 if e.code == G.GEMM_ERR_INIT else 1
 
 
+# ---- peak probe (tune/peak.swift, `./run_tune.sh peak`) ------------------------------------
+PEAK_KINDS = [(0, "tcgen05 kind::f16"), (1, "tcgen05 kind::i8"), (2, "tcgen05 kind::f8f6f4"),
+              (3, "tcgen05 kind::mxf8f6f4"), (4, "tcgen05 kind::mxf4"), (5, "tcgen05 kind::f16 x2"),
+              (6, "tcgen05 kind::i8 x2"), (7, "tcgen05 kind::f8f6f4 x2")]
+PEAK_REPS = 4096
+
+
+def run_peak(a) -> int:
+    """Dense tensor-core peak per MMA kind: MMAs on operands resident in shared
+    memory, no DRAM traffic (tune/peak.metal:29-87, host tune/peak.swift:31-65).
+    `x2` rows use CTA pairs (cta_group::2).  --iters sets the timed launches
+    (median reported); the reference's default is 10."""
+    if G.device_count() < 1:
+        raise BenchExit(1, "No CUDA device")
+    G.init(0)
+    name, _, sms = G.device_info(0)
+    iters = a.iters if a.shape_set else 10
+    print(f"device: {name}  ctas={sms} R={PEAK_REPS}")
+    print("%-28s %12s" % ("kernel", "TFLOPS/TOPS"))
+    for kind, label in PEAK_KINDS:
+        print("%-28s %12.1f" % (label, G.peak_probe(0, kind, PEAK_REPS, iters)))
+    sys.stdout.flush()
+    return 0
+
+
 def _main(argv) -> int:
     try:
         tiles = G.tile_names()
     except G.GemmError as e:
         raise BenchExit(2, f"Failed loading libgemm.so: {e}")
     a = parse_args(argv, tiles)
+    if a.peak:
+        return run_peak(a)
     shapes = shapes_for(a)
     for s in shapes:
         if s.N <= 0 or s.K <= 0 or s.M <= 0 or s.iters <= 0:

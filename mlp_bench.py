@@ -6,6 +6,7 @@
                         [--autotune] [--no-profile]
                         [--gpus 1|2|4|8] [--allgather] [--data ref|seeded]
                         [--seed s] [--rotate r] [--flush]
+    python mlp_bench.py --peak [--iters i]     (tensor-core peak per MMA kind)
 
 With --gpus N > 1 launch it under torchrun (one process per GPU):
     torchrun --nproc-per-node N --master-addr 127.0.0.1 mlp_bench.py --gpus N ...

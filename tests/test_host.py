@@ -91,6 +91,8 @@ def test_parse_args_quirks():
     with pytest.raises(D.BenchExit) as e:
         D.parse_args(["--tile", "64x32"], tiles)
     assert e.value.code == 1 and "Unknown --tile 64x32" in e.value.msg
+    a = D.parse_args(["--peak", "--iters", "3"], tiles)     # peak probe mode (tune/peak.swift)
+    assert a.peak and a.iters == 3 and not a.suite
 
 
 def test_sample_points_match_oracle():
