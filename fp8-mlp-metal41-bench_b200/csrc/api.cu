@@ -461,4 +461,23 @@ int gemm_peak_probe(int device, int kind, int reps, int iters, double* tflops_ou
   return rc;
 }
 
+int gemm_quantize(int device, int format, const float* src, void* dst, void* scales, long rows, long cols,
+                  void* stream) {
+  DevState* s = dev_state(device);
+  if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised", device);
+  if (format < GEMM_Q_E4M3_REF || format > GEMM_Q_MXFP8) return fail(GEMM_ERR_ARGS, "unknown format %d", format);
+  if (rows <= 0 || cols <= 0 || !src || !dst) return fail(GEMM_ERR_ARGS, "bad quantiser arguments");
+  const bool mx = format == GEMM_Q_MXFP4 || format == GEMM_Q_MXFP8;
+  if (mx && (cols % 32 != 0 || !scales))
+    return fail(GEMM_ERR_ARGS, "MX formats need cols %% 32 == 0 and a scale plane");
+  if ((format == GEMM_Q_E2M1 || format == GEMM_Q_MXFP4) && (rows * cols) % 2 != 0)
+    return fail(GEMM_ERR_ARGS, "E2M1 packs two per byte: rows*cols must be even");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+  e = launch_quant(format, src, dst, scales, rows, cols, s->num_sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "quantiser launch");
+  return GEMM_OK;
+}
+
 }  // extern "C"

@@ -50,6 +50,10 @@ cudaError_t launch_l2_flush(const void* buf, size_t bytes, int num_sms, cudaStre
 // Record a message for gemm_last_error() (defined in api.cu).
 void set_last_error(const char* msg);
 
+// ---- quantisers (quant.cu): GEMM_Q_* formats of the public header ------------------
+cudaError_t launch_quant(int format, const float* src, void* dst, void* scales, long rows, long cols,
+                         int num_sms, cudaStream_t st);
+
 // ---- peak probe -----------------------------------------------------------------
 cudaError_t launch_peak(int kind, int reps, int ctas, float* sink, int* dev_err,
                         cudaStream_t st);

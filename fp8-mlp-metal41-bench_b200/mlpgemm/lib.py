@@ -23,7 +23,11 @@ EXPORTS = [
     "gemm_workspace_size", "gemm_alloc", "gemm_free", "gemm_memset", "gemm_h2d", "gemm_d2h",
     "gemm_host_alloc", "gemm_host_free", "gemm_run", "gemm_sync", "gemm_time",
     "gemm_time_e2e", "gemm_launches_per_run", "gemm_peak_probe", "gemm_run_noalloc",
+    "gemm_quantize",
 ]
+
+# quantiser formats (GEMM_Q_* in include/mlpgemm.h)
+Q_E4M3_REF, Q_E4M3, Q_E2M1, Q_MXFP4, Q_MXFP8 = 0, 1, 2, 3, 4
 
 
 class GemmError(RuntimeError):
@@ -80,6 +84,7 @@ def _declare(L):
         "gemm_peak_probe": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
         "gemm_run_noalloc": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp,
                                      vp]),
+        "gemm_quantize": (c_int, [c_int, c_int, vp, vp, vp, ctypes.c_long, ctypes.c_long, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -270,3 +275,9 @@ def peak_probe(device: int, kind: int, reps: int = 4096, iters: int = 10) -> flo
     v = ctypes.c_double(0.0)
     check(lib().gemm_peak_probe(device, kind, reps, iters, ctypes.byref(v)), "gemm_peak_probe")
     return v.value
+
+
+def quantize(device, fmt, src, dst, scales=None, rows=1, cols=1, stream=None) -> None:
+    """f32 [rows, cols] on the device -> a GEMM_Q_* format in `dst` (+ UE8M0 `scales`)."""
+    check(lib().gemm_quantize(device, fmt, as_ptr(src), as_ptr(dst), as_ptr(scales), int(rows), int(cols),
+                              as_ptr(stream)), "gemm_quantize")

@@ -193,6 +193,31 @@ int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const voi
  * few hundred bytes of device memory for its result sink. */
 int gemm_peak_probe(int device, int kind, int reps, int iters, double *tflops_out);
 
+/* ---- quantisers: the operand formats produced from f32 on the device ---------
+ * Replaces the reference's host-side producers, which run untimed before the
+ * buffers are made (main.swift:6-27 floatToE4M3, :50-67 E2M1 codes packed two
+ * per byte with the low nibble the even element, :76-83 UE8M0 codes).
+ * src is f32 [rows, cols] on the device; dst receives:
+ *   GEMM_Q_E4M3_REF  one byte per element, floatToE4M3 bit for bit
+ *   GEMM_Q_E4M3      one byte per element, OCP E4M3FN round-to-nearest-even
+ *                    with subnormals, saturating at +-448, NaN -> 0x7F
+ *   GEMM_Q_E2M1      two per byte (rows*cols even), round-to-nearest-even,
+ *                    saturating at +-6, NaN -> 0x7
+ *   GEMM_Q_MXFP4     OCP MX: E2M1 two per byte plus one UE8M0 code per 32
+ *   GEMM_Q_MXFP8     OCP MX: one E4M3 byte per element plus one UE8M0 per 32
+ * For the MX formats cols % 32 == 0 and `scales` receives [rows, cols/32]:
+ * X = floor(log2(max |v| of the 32)) - emax (2 for E2M1, 8 for E4M3) clamped to
+ * [-127, 127], code X + 127, elements quantised from v * 2^-X; a block of
+ * zeros gets code 0, a block holding NaN or Inf code 0xFF and zero elements.
+ * Asynchronous on `stream` (NULL: the device's library stream). */
+#define GEMM_Q_E4M3_REF 0
+#define GEMM_Q_E4M3     1
+#define GEMM_Q_E2M1     2
+#define GEMM_Q_MXFP4    3
+#define GEMM_Q_MXFP8    4
+int gemm_quantize(int device, int format, const float *src, void *dst, void *scales,
+                  long rows, long cols, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

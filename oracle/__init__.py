@@ -69,6 +69,10 @@ def lib() -> ctypes.CDLL:
         L.orc_e2m1_at.argtypes = [vp, c_long]
         L.orc_pack_e2m1.restype = None
         L.orc_pack_e2m1.argtypes = [vp, c_long, vp]
+        L.orc_f32_to_e2m1_rne.restype = ctypes.c_uint8
+        L.orc_f32_to_e2m1_rne.argtypes = [ctypes.c_float]
+        L.orc_quantize_mx.restype = c_int
+        L.orc_quantize_mx.argtypes = [c_int, vp, c_long, c_long, vp, vp]
         L.orc_check_layout.restype = c_int
         L.orc_check_layout.argtypes = [c_int, c_long, c_long, c_long]
         L.orc_decode_x.restype = c_int
@@ -126,6 +130,24 @@ def f32_to_e4m3_ref(x: float) -> int:
 
 def f32_to_e4m3_rne(x: float) -> int:
     return lib().orc_f32_to_e4m3_rne(x)
+
+
+def f32_to_e2m1_rne(x: float) -> int:
+    return lib().orc_f32_to_e2m1_rne(x)
+
+
+def quantize_mx(elem: int, src: np.ndarray):
+    """OCP MX block quantisation of a [rows, cols] f32 array (cols % 32 == 0):
+    elem 0 -> (E2M1 packed [rows, cols/2], UE8M0 [rows, cols/32]); elem 1 ->
+    (E4M3 [rows, cols], UE8M0 [rows, cols/32])."""
+    src = np.ascontiguousarray(src, dtype=np.float32)
+    rows, cols = src.shape
+    vals = np.zeros((rows, cols // 2 if elem == 0 else cols), dtype=np.uint8)
+    scales = np.zeros((rows, cols // 32), dtype=np.uint8)
+    rc = lib().orc_quantize_mx(elem, src.ctypes.data, rows, cols, vals.ctypes.data, scales.ctypes.data)
+    if rc:
+        raise ValueError("quantize_mx: cols must be a multiple of 32")
+    return vals, scales
 
 
 def e2m1_to_e4m3_byte(n: int) -> int:

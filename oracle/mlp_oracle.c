@@ -160,6 +160,73 @@ void orc_pack_e2m1(const uint8_t *codes, long count, uint8_t *out)
     }
 }
 
+/* OCP E2M1 from f32: round to nearest, ties to the even code, on the grid
+ * {0, .5, 1, 1.5, 2, 3, 4, 6}; |x| > 6 and Inf saturate to 6; NaN -> 0x7.
+ * Below 2 the grid step is 0.5, in [2, 4) it is 1, from 4 on it is 2. */
+uint8_t orc_f32_to_e2m1_rne(float x)
+{
+    if (isnan(x)) return 0x7;
+    uint8_t sign = signbit(x) ? 0x8 : 0;
+    double ax = fabs((double)x);
+    int code;
+    if (ax >= 6.0) {
+        code = 7;                                 /* 6, larger values and Inf saturate */
+    } else if (ax < 2.0) {
+        code = (int)nearbyint(ax * 2.0);          /* 0..4 -> 0, .5, 1, 1.5, 2 */
+    } else if (ax < 4.0) {
+        int q = (int)nearbyint(ax);               /* 2..4 */
+        code = q == 2 ? 4 : q == 3 ? 5 : 6;
+    } else {
+        int q = (int)nearbyint(ax / 2.0);         /* 2.. (4, 6, then saturation) */
+        code = q <= 2 ? 6 : 7;
+    }
+    return (uint8_t)(sign | code);
+}
+
+/* OCP MX block quantisation (see the header for the exact rules). */
+int orc_quantize_mx(int elem, const float *src, long rows, long cols, uint8_t *vals, uint8_t *scales)
+{
+    if (rows <= 0 || cols <= 0 || cols % 32 != 0 || (elem != 0 && elem != 1)) return 1;
+    const int emax = elem == 0 ? 2 : 8;
+    long nb = cols / 32;
+    if (elem == 0) for (long i = 0; i < rows * cols / 2; ++i) vals[i] = 0;
+    for (long r = 0; r < rows; ++r) {
+        for (long b = 0; b < nb; ++b) {
+            const float *v = src + r * cols + b * 32;
+            int bad = 0;
+            float amax = 0.0f;
+            for (int i = 0; i < 32; ++i) {
+                if (!isfinite(v[i])) bad = 1;
+                else if (fabsf(v[i]) > amax) amax = fabsf(v[i]);
+            }
+            int X;
+            uint8_t code;
+            if (bad) { code = 0xFF; X = 0; }
+            else if (amax == 0.0f) { code = 0; X = -127; }
+            else {
+                int e2;
+                frexpf(amax, &e2);                    /* amax in [2^(e2-1), 2^e2) */
+                X = (e2 - 1) - emax;
+                if (X < -127) X = -127;
+                if (X > 127) X = 127;
+                code = (uint8_t)(X + 127);
+            }
+            scales[r * nb + b] = code;
+            for (int i = 0; i < 32; ++i) {
+                uint8_t q = 0;
+                if (!bad) {
+                    float s = ldexpf(v[i], -X);       /* exact: a power-of-two scaling */
+                    q = elem == 0 ? orc_f32_to_e2m1_rne(s) : orc_f32_to_e4m3_rne(s);
+                }
+                long idx = r * cols + b * 32 + i;
+                if (elem == 0) vals[idx / 2] |= (idx % 2 == 0) ? q : (uint8_t)(q << 4);
+                else vals[idx] = q;
+            }
+        }
+    }
+    return 0;
+}
+
 /* e2m1At, main.swift:69-73. */
 float orc_e2m1_at(const uint8_t *packed, long index)
 {

@@ -54,6 +54,20 @@ uint8_t  orc_ue8m0_code(long i);              /* main.swift:80-83             */
 uint8_t  orc_e2m1_to_e4m3_byte(uint8_t nibble); /* fp8_mlp.metal:305-309 LUT  */
 void     orc_pack_e2m1(const uint8_t *codes, long count, uint8_t *out); /* :56-67 */
 
+/* ---- quantisers (the wire formats produced from f32) ----------------------
+ * E4M3: orc_f32_to_e4m3_ref / _rne above.  E2M1: OCP round to nearest even on
+ * {0, .5, 1, 1.5, 2, 3, 4, 6}, saturating at +-6, sign kept (also for -0);
+ * NaN -> 0x7.  MX (OCP MX v1.0 block scaling), one UE8M0 scale per 32
+ * consecutive elements of a row: X = floor(log2(amax)) - emax (emax 2 for
+ * E2M1, 8 for E4M3) clamped to [-127, 127], scale code X + 127, elements
+ * quantised (RNE, saturating) from v * 2^-X.  amax == 0 gives code 0 and zero
+ * elements; a block holding NaN or Inf gets scale code 0xFF (NaN) and zero
+ * elements.  elem 0: E2M1 packed two per byte along the row (low nibble =
+ * even element, main.swift:56-67); elem 1: one E4M3 byte per element. */
+uint8_t  orc_f32_to_e2m1_rne(float x);
+int      orc_quantize_mx(int elem, const float *src, long rows, long cols,
+                         uint8_t *vals, uint8_t *scales);
+
 /* ---- operand decode (main.swift:419-449) ---------------------------------
  * X: the activation buffer the dtype uses (main.swift:477-483); xscale is the
  * [N, K/32] UE8M0 plane (mxfp4/a4, mxfp4/a8 only, else NULL).
