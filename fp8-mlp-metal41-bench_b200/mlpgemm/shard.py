@@ -19,7 +19,12 @@ no exchange inside it:
     per-GPU median time;
   * --allgather gathers the Y blocks over NCCL (NVLink) into [G, N, w] and
     lays them out as [N, M] on every GPU; that collective is timed
-    separately (`allgather_ms`) and does not enter the GEMM rate.
+    separately (`allgather_ms`) and does not enter the GEMM rate;
+  * with --allgather the GEMM and the gather also run as a stream-level
+    pipeline (`pipeline_ms`): the rank's block is computed in row chunks of
+    Y on one CUDA stream, and each finished chunk is all-gathered by NCCL on
+    a second stream while the next chunk computes.  The pipeline's own
+    end-to-end time is reported beside gemm + all-gather run back to back.
 
 torch.distributed is plumbing here (device buffers, NCCL, barriers); the
 GEMM itself is libgemm.so through its C ABI.
@@ -68,6 +73,21 @@ def shard_plan(M: int, world: int):
     return out
 
 
+def row_chunks(N: int, chunks: int):
+    """[n0, n1) row ranges of Y for the GEMM / all-gather pipeline: `chunks`
+    nearly equal parts, each a multiple of 128 rows (one tensor-core tile
+    row) except the last, never empty."""
+    if N <= 128 or chunks <= 1:
+        return [(0, N)]
+    per = -(-N // chunks)
+    per = -(-per // 128) * 128
+    out, n0 = [], 0
+    while n0 < N:
+        out.append((n0, min(N, n0 + per)))
+        n0 += per
+    return out
+
+
 def _x_bytes_tensor(torch, ops: Operands, dtype: str, device):
     x = ops.X(dtype)
     return torch.from_numpy(x.view(np.uint8).copy()).to(device)
@@ -82,6 +102,7 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
     m0, width = plan[rank]
     dev = torch.device("cuda", local)
     medians = {}
+    extra_pipe = {}
     for dtype in a.dtypes:
         if not F.layout_ok(dtype, N, K, M):
             raise BenchExit(1, f"{dtype} needs even X/W counts and K a multiple of 32 "
@@ -144,18 +165,21 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
             if width > 0:
                 Ypad.view(N, wmax)[:, :width].copy_(Y.view(N, width))
             out = torch.empty(world * N * wmax, dtype=Y.dtype, device=dev)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            dist.all_gather_into_tensor(out, Ypad)
             full = torch.empty(N, M, dtype=Y.dtype, device=dev)
             blocks = out.view(world, N, wmax)
-            for g, (g0, gw) in enumerate(plan):
-                if gw:
-                    full[:, g0:g0 + gw].copy_(blocks[g, :, :gw])
-            e1.record()
-            torch.cuda.synchronize()
-            ag_ms = e0.elapsed_time(e1)
+            times = []
+            for _ in range(6):   # one warm-up (NCCL sets up its buffers), then the median of 5
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                dist.all_gather_into_tensor(out, Ypad)
+                for g, (g0, gw) in enumerate(plan):
+                    if gw:
+                        full[:, g0:g0 + gw].copy_(blocks[g, :, :gw])
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ag_ms = sorted(times[1:])[2]
             t = torch.tensor([ag_ms], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ag_ms = float(t.item())
@@ -163,6 +187,9 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
                 for g, (g0, gw) in enumerate(plan):
                     if gw:
                         assert torch.equal(full[:, g0:g0 + gw], blocks[g, :, :gw])
+            pipe_ms = _pipeline(a, torch, dist, world, local, dt, ti, tile, X, XS, Wt, WS, WSP, wsb,
+                                dtype, N, K, width, wmax, Y, full, plan)
+            extra_pipe[dtype] = pipe_ms
         if dtype == "fp16":
             vs = "1.000"
         elif "fp16" in medians:
@@ -171,8 +198,55 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
             vs = "-"
         rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
                         rel, gpus=world, allgather_ms=ag_ms))
-        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, width))
+        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, width, med_max * 1000.0,
+                      extra_pipe.get(dtype)))
     return rows, extra
+
+
+def _pipeline(a, torch, dist, world, local, dt, ti, tile, X, XS, Wt, WS, WSP, wsb, dtype, N, K, width, wmax,
+              Y, full_ref, plan, chunks=4, reps=5):
+    """GEMM in row chunks of Y on one stream, each chunk all-gathered over NCCL
+    on a second stream as soon as it is done; returns the median over `reps`
+    of the max over ranks of the end-to-end event time (ms)."""
+    dev = torch.device("cuda", local)
+    # packed 4-bit X rows start on a byte only for even K
+    parts = row_chunks(N, chunks) if not (dtype in F.X_FP4 and K % 2) else [(0, N)]
+    xrow = F.x_bytes(dtype, 1, K)   # bytes per X row
+    es = Y.element_size()
+    ys = [torch.zeros(n1 - n0, wmax, dtype=Y.dtype, device=dev) for n0, n1 in parts]
+    outs = [torch.empty(world * (n1 - n0) * wmax, dtype=Y.dtype, device=dev) for n0, n1 in parts]
+    gemm_s, comm_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    cur = torch.cuda.current_stream(dev)
+    times = []
+    for _ in range(reps + 1):
+        gemm_s.wait_stream(cur)
+        comm_s.wait_stream(cur)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(gemm_s)
+        comm_s.wait_event(e0)
+        for c, (n0, n1) in enumerate(parts):
+            if width > 0:
+                xs_ptr = None if XS is None else XS.data_ptr() + n0 * (K // 32)
+                G.run(local, dt, ti, X.data_ptr() + n0 * xrow, Wt, ys[c].data_ptr(), n1 - n0, K, width,
+                      xs_ptr, WS, WSP, wsb, stream=gemm_s.cuda_stream)
+            done = torch.cuda.Event()
+            done.record(gemm_s)
+            comm_s.wait_event(done)
+            with torch.cuda.stream(comm_s):
+                dist.all_gather_into_tensor(outs[c], ys[c])
+        e1.record(comm_s)
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1))
+    # the pipelined result equals the one gathered in one piece
+    for c, (n0, n1) in enumerate(parts):
+        blocks = outs[c].view(world, n1 - n0, wmax)
+        for g, (g0, gw) in enumerate(plan):
+            if gw:
+                assert torch.equal(blocks[g, :, :gw], full_ref[n0:n1, g0:g0 + gw])
+    med = sorted(times[1:])[len(times[1:]) // 2]
+    t = torch.tensor([med], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 class _SubOps:
@@ -227,12 +301,15 @@ def main_sharded(a, shapes) -> int:
             print(line)
         print("")
         hdr = " ".join([_c("shape", 8), _c("dtype", 9), _c("gpus", 4, True), _c("cols/gpu", 8, True),
-                        _c("bcast_ms", 10, True), _c("allgather_ms", 12, True)])
+                        _c("bcast_ms", 10, True), _c("allgather_ms", 12, True),
+                        _c("gemm+ag_ms", 11, True), _c("pipeline_ms", 11, True)])
         print(hdr)
         print("-" * len(hdr))
-        for (sh, d, g, b, ag, w) in extra:
+        for (sh, d, g, b, ag, w, gm, pp) in extra:
+            seq = "-" if ag is None else "%.4f" % (gm + ag)
             print(" ".join([_c(sh, 8), _c(d, 9), _c(str(g), 4, True), _c(str(w), 8, True),
-                            _c("%.4f" % b, 10, True), _c("-" if ag is None else "%.4f" % ag, 12, True)]))
+                            _c("%.4f" % b, 10, True), _c("-" if ag is None else "%.4f" % ag, 12, True),
+                            _c(seq, 11, True), _c("-" if pp is None else "%.4f" % pp, 11, True)]))
         print("ok")
         sys.stdout.flush()
     return 0
@@ -243,4 +320,4 @@ def _c(t, w, right=False):
     return p + t if right else t + p
 
 
-__all__ = ["main_sharded", "shard_plan", "table_line"]
+__all__ = ["main_sharded", "shard_plan", "row_chunks", "table_line"]

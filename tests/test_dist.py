@@ -64,5 +64,18 @@ def test_shard_plan_covers_columns():
     assert shard_plan(11008, 8) == [(i * 1376, 1376) for i in range(8)]
 
 
+def test_pipeline_row_chunks():
+    from mlpgemm.shard import row_chunks
+    for N in (1, 100, 128, 129, 2048, 4096, 1000):
+        for c in (1, 2, 4, 8):
+            parts = row_chunks(N, c)
+            assert parts[0][0] == 0 and parts[-1][1] == N
+            assert all(a < b for a, b in parts)
+            assert all(parts[i][1] == parts[i + 1][0] for i in range(len(parts) - 1))
+            assert all((b - a) % 128 == 0 for a, b in parts[:-1])
+            assert len(parts) <= max(1, c)
+    assert row_chunks(2048, 4) == [(0, 512), (512, 1024), (1024, 1536), (1536, 2048)]
+
+
 def test_strong_scaling_rate():
     assert DU.strong_scaling_rate(2.0, 1.0) == pytest.approx(2e-9)
