@@ -162,13 +162,17 @@ struct Cfg {
   static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
-  // TMEM: [0, 2*BN) accumulators; then per stage and cell 4 columns for A and
-  // 4*BN/128 for B (one 32-bit column per 32 rows, byte s = block s)
+  // TMEM: [0, ACC_BUFS*BN) accumulators; then per stage and cell 4 columns for
+  // A and 4*BN/128 for B (one 32-bit column per 32 rows, byte s = block s).
+  // Block-scaled 256-wide tiles keep one accumulator: two would fill all 512
+  // columns and leave none for the scale cells (the epilogue then drains the
+  // accumulator before the next tile's first MMA).
+  static constexpr int ACC_BUFS = (SCALED && BN == 256) ? 1 : 2;
   static constexpr int ACC_COLS = BN;
-  static constexpr int SF_COL0 = 2 * BN;
+  static constexpr int SF_COL0 = ACC_BUFS * BN;
   static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
   static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
-  static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN + STAGES * SF_COLS_STAGE);
+  static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + STAGES * SF_COLS_STAGE);
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
   static constexpr uint32_t IDESC =
@@ -179,7 +183,7 @@ struct Cfg {
                 ((uint32_t)(kBM >> 4) << 24));
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
   static_assert(!T::b_mn || BN % B_BOX_MN == 0, "MN-major B tile must be whole swizzle atoms");
-  static_assert(2 * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
+  static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
@@ -350,8 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-      const int buf = local & 1;
-      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
+      const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       if (!mbar_wait(&bars->acc_empty[buf], acc_par ^ 1u, ctl, 0x200 + buf)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * C::ACC_COLS);
@@ -407,8 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, tm, tn);
-      const int buf = local & 1;
-      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
+      const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       const bool got = mbar_wait(&bars->acc_full[buf], acc_par, ctl, 0x400 + buf);
       if (!__all_sync(0xffffffffu, got)) break;   // the warp leaves together
       __syncwarp();                               // tcgen05.ld is .sync.aligned
@@ -1333,10 +1337,10 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
     case kFP16: return K % 8 == 0 && M % 8 == 0;
     case kI8I8:
     case kF8F8: return K % 16 == 0 && M % 16 == 0;
-    case kMX4X4: return bn == 128 && K % 32 == 0;
-    case kF4F4: return bn == 128 && K % 32 == 0 && M % 2 == 0;
+    case kMX4X4: return K % 32 == 0;
+    case kF4F4: return K % 32 == 0 && M % 2 == 0;
     case kMX8X4:
-    case kF8X4: return bn == 128 && K % 128 == 0;
+    case kF8X4: return K % 128 == 0;
     case kINT8:
     case kFP8: return K % 8 == 0 && M % 16 == 0;
     case kMXFP4: return K % 32 == 0;
@@ -1449,10 +1453,10 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
       if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
       return bn == 256 ? launch_widen<kMXFP4, 256, 3>(a) : launch_widen<kMXFP4, 128, 5>(a);
     }
-    case kMX4X4: return launch_scaled<kMX4X4, 128, 5>(a);
-    case kMX8X4: return launch_scaled<kMX8X4, 128, 5>(a);
-    case kF8X4: return launch_scaled<kF8X4, 128, 5>(a);
-    case kF4F4: return launch_scaled<kF4F4, 128, 5>(a);
+    case kMX4X4: return bn == 256 ? launch_scaled<kMX4X4, 256, 4>(a) : launch_scaled<kMX4X4, 128, 5>(a);
+    case kMX8X4: return bn == 256 ? launch_scaled<kMX8X4, 256, 4>(a) : launch_scaled<kMX8X4, 128, 5>(a);
+    case kF8X4: return bn == 256 ? launch_scaled<kF8X4, 256, 4>(a) : launch_scaled<kF8X4, 128, 5>(a);
+    case kF4F4: return bn == 256 ? launch_scaled<kF4F4, 256, 4>(a) : launch_scaled<kF4F4, 128, 5>(a);
     default: return cudaErrorInvalidValue;
   }
 }
