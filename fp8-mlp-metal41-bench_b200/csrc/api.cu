@@ -252,6 +252,10 @@ int gemm_check_layout(int dtype, int N, int K, int M) {
 int gemm_default_tile(int dtype, int N, int K, int M) {
   if (layout_check(dtype, N, K, M) != GEMM_OK) return -1;
   if (N > 16) {
+    // block-scaled kinds: the 1-CTA 128x256 tile measures ahead of the CTA pair
+    // (which keeps one accumulator in TMEM next to its scale cells)
+    const bool scaled = dtype == kMX4X4 || dtype == kMX8X4 || dtype == kF8X4;
+    if (scaled && tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
     if (tc_supported(dtype, 256, 256, N, K, M)) return gemm_tile_index("256x256");
     if (tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
     if (tc_supported(dtype, 128, 128, N, K, M)) return gemm_tile_index("128x128");

@@ -530,9 +530,24 @@ struct Cfg2 {
   static constexpr int A_BYTES = kBM * kRowBytes;
   static constexpr int B_BYTES = BH * kRowBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // transaction bytes: the 16U4_ALIGN16B loads count the packed 4-bit source
-  static constexpr bool UNPACK4 = DT == kF4F4Pair;
-  static constexpr int STAGE_TX = UNPACK4 ? STAGE_BYTES / 2 : STAGE_BYTES;
+  // 4-bit operands unpacked into 8-bit containers by TMA (16U4_ALIGN16B); those
+  // loads count the packed source bytes, half of what they write
+  static constexpr bool A_UNPACK = DT == kF4F4Pair;
+  static constexpr bool B_UNPACK = DT == kF4F4Pair || T::b_unpack4;
+  static constexpr int STAGE_TX = (A_UNPACK ? A_BYTES / 2 : A_BYTES) + (B_UNPACK ? B_BYTES / 2 : B_BYTES);
+  // block-scaled kinds: per stage SF_CELLS 512-byte scale blocks for this CTA's
+  // 128 rows of A and for all BN columns of B (each CTA's TMEM holds the scales
+  // of every column the pair's MMA multiplies its rows with), as in Cfg
+  static constexpr bool SCALED = T::nsf > 0;
+  static constexpr int SF_CELLS = SCALED ? (kRowBytes / 32) * T::nsf / 4 : 0;
+  static constexpr int SF_B_CHUNKS = BN / 128;
+  static constexpr int SF_A_BYTES = SF_CELLS * kSfChunk;
+  static constexpr int SF_B_BYTES = SF_CELLS * SF_B_CHUNKS * kSfChunk;
+  static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
+  static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
+  static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
+  // one accumulator when scaled: two 256-column ones would leave no TMEM for scales
+  static constexpr int ACC_BUFS = SCALED ? 1 : 2;
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;
   static constexpr int MMA_K_BYTES = 32;
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;
@@ -542,13 +557,18 @@ struct Cfg2 {
   static constexpr uint32_t B_LBO = T::b_mn ? (uint32_t)B_BOX_BYTES : 16u;
   static constexpr uint32_t B_ADV = T::b_mn ? (uint32_t)(MMA_K_BYTES * 8 / T::b_bits) * kRowBytes
                                             : (uint32_t)MMA_K_BYTES;
-  static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN);
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SF_COL0 = ACC_BUFS * BN;
+  static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + STAGES * SF_COLS_STAGE);
+  static constexpr int SF_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
+  static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
   static constexpr uint32_t IDESC =
-      (T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | ((T::b_mn ? 1u : 0u) << 16) |
-      ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-  static_assert(T::nsf == 0, "block-scaled kinds use the 1-CTA kernel");
+      SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
+                ((uint32_t)(256 >> 4) << 24))
+             : ((T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | ((T::b_mn ? 1u : 0u) << 16) |
+                ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24));
+  static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
   static_assert(!T::b_mn || BH % B_BOX_MN == 0, "W half-tile must be whole swizzle atoms");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -556,6 +576,7 @@ struct Cfg2 {
 template <int DT, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
                         TcParams p) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
@@ -583,6 +604,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
+  if constexpr (C::SCALED) {
+    // 512 bytes of UE8M0 127 (scale 1) for an operand without a scale plane
+    if (warp == 2)
+      *reinterpret_cast<uint4*>(smem + C::SF_CONST_OFF + lane * 16) =
+          make_uint4(0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
+    fence_proxy_async_smem();
+  }
   if (warp == 1) {
     tmem_alloc_pair(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish_pair();
@@ -597,6 +625,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------ TMA producer (both CTAs) ------------------------
     uint32_t stage = 0, phase = 0;
     bool ok = true;
+    // bytes each CTA lands per stage (the leader expects both CTAs' on its barrier)
+    const uint32_t tx = C::STAGE_TX + (C::SCALED ? (p.sfa ? C::SF_A_BYTES : 0) + (p.sfb ? C::SF_B_BYTES : 0) : 0);
+    if constexpr (C::SCALED) {
+      tma_prefetch_desc(&tmSA);
+      tma_prefetch_desc(&tmSB);
+    }
     for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, tm, tn);
@@ -608,18 +642,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Only the leader arrives, expecting both CTAs' bytes; the peer's loads
         // just complete their transactions on the leader's barrier (a remote
         // arrive per stage would put a cross-SM round trip in the peer's loop).
-        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * C::STAGE_TX);
+        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * tx);
         // x counts elements of the map: 16-bit or 4-bit (unpacking maps) elements, else bytes
         tma_load_2d_pair(a_dst, &tmA, lfull,
-                         kb * ((T::a_bits == 16 || C::UNPACK4) ? C::K_PER_STAGE : kRowBytes),
+                         kb * ((T::a_bits == 16 || C::A_UNPACK) ? C::K_PER_STAGE : kRowBytes),
                          tm * 256 + (int)rank * kBM);
+        if constexpr (C::SCALED) {
+          // packed scale blocks: rows of 512 bytes, [128-row tile][stage][cell]
+          unsigned char* sf = smem + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+          if (p.sfa)
+            tma_load_2d_pair(sf, &tmSA, lfull, 0, ((2 * tm + (int)rank) * p.num_kb + kb) * C::SF_CELLS);
+          if (p.sfb) {
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tma_load_2d_pair(sf + C::SF_A_BYTES + c * C::SF_A_BYTES, &tmSB, lfull, 0,
+                               ((tn * C::SF_B_CHUNKS + c) * p.num_kb + kb) * C::SF_CELLS);
+          }
+        }
         if constexpr (T::b_mn) {
 #pragma unroll
           for (int j = 0; j < C::B_BOXES; ++j)
             tma_load_2d_pair(b_dst + j * C::B_BOX_BYTES, &tmB, lfull, tn * BN + (int)rank * C::BH + j * C::B_BOX_MN,
                              kb * C::K_PER_STAGE);
         } else {
-          tma_load_2d_pair(b_dst, &tmB, lfull, kb * (C::UNPACK4 ? C::K_PER_STAGE : kRowBytes),
+          tma_load_2d_pair(b_dst, &tmB, lfull, kb * (C::B_UNPACK ? C::K_PER_STAGE : kRowBytes),
                            tn * BN + (int)rank * C::BH);
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -633,8 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
     for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
-      const int buf = local & 1;
-      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
+      const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       if (!mbar_wait(&bars->acc_empty[buf], acc_par ^ 1u, ctl, 0x200 + buf)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
@@ -643,11 +689,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
         const uint32_t b_addr = a_addr + C::A_BYTES;
+        if constexpr (C::SCALED) {
+          // each CTA's scale blocks of this stage -> its own TMEM (one copy per cell)
+          const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
+          const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
+          const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
-        for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
-          const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
-          const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
-          tc_mma_pair<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          for (int g = 0; g < C::SF_CELLS; ++g) {
+            const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+            tc_cp_pair_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + g * kSfChunk : sf_const, 0, 128));
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_pair_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
+                                        sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
+                                                          : sf_const, 0, 128));
+          }
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            constexpr int per_cell = 4 / T::nsf;
+            const int g = kk / per_cell;
+            const uint32_t sfid = (uint32_t)((kk % per_cell) * T::nsf);
+            const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+            const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+            tc_mma_pair_bs<T::kind>(d_tmem, adesc, bdesc, C::IDESC | (sfid << 4) | (sfid << 29),
+                                    (kb | kk) != 0 ? 1u : 0u, sfa_t, sfa_t + C::SF_COLS_A);
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
+            const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
+            const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
+            tc_mma_pair<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
         }
         tc_commit_pair(&bars->empty[stage], 0x3);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -663,8 +737,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, tm, tn);
-      const int buf = local & 1;
-      const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
+      const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       const bool got = mbar_wait(&bars->acc_full[buf], acc_par, ctl, 0x400 + buf);
       if (!__all_sync(0xffffffffu, got)) { aborted_any = true; break; }
       __syncwarp();
@@ -1135,6 +1209,20 @@ bool make_map_plain(CUtensorMap* m, const void* base, uint64_t inner, uint64_t o
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Packed scale blocks (sf_pack_kernel output) as a 2-D map: `rows` rows of
+// 128 x 32-bit (one 512-byte block each), boxes of `cells` rows, no swizzle.
+bool make_map_sf(CUtensorMap* m, const void* base, uint64_t rows, uint32_t cells) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {128, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kSfChunk};
+  cuuint32_t box[2] = {128, cells};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int current_device() {
   int d = 0;
   cudaGetDevice(&d);
@@ -1197,19 +1285,17 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
 }
 
 template <int DT, int BN, int STAGES>
-cudaError_t launch_pair(const RunArgs& a, const void* W) {
+cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nullptr, const uint8_t* sfb = nullptr,
+                        int sf_rows_a = 0, int sf_rows_b = 0) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmSA, tmSB;
   const CUtensorMapDataType ty8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok;
-  if constexpr (C::UNPACK4) {
+  if constexpr (C::A_UNPACK) {
     // packed E2M1 rows of K/2 bytes, unpacked to one byte per element in shared memory
     ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.N,
-                  (uint64_t)a.K / 2, C::K_PER_STAGE, kBM) &&
-         make_map(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.M,
-                  (uint64_t)a.K / 2, C::K_PER_STAGE, C::BH);
-    if (!ok) return cudaErrorInvalidValue;
+                  (uint64_t)a.K / 2, C::K_PER_STAGE, kBM);
   } else if constexpr (T::a_bits == 16) {
     ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K * 2,
                   C::K_PER_STAGE, kBM);
@@ -1218,8 +1304,9 @@ cudaError_t launch_pair(const RunArgs& a, const void* W) {
     ok = make_map(&tmA, a.X, ty8, row_bytes, (uint64_t)a.N, row_bytes, kRowBytes, kBM);
   }
   if (!ok) return cudaErrorInvalidValue;
-  if constexpr (C::UNPACK4) {
-    // tmB made above
+  if constexpr (C::B_UNPACK) {
+    ok = make_map(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.M,
+                  (uint64_t)a.K / 2, C::K_PER_STAGE, C::BH);
   } else if constexpr (T::b_mn) {
     const int es = T::b_bits / 8;
     ok = make_map(&tmB, W, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : ty8, (uint64_t)a.M, (uint64_t)a.K,
@@ -1229,10 +1316,17 @@ cudaError_t launch_pair(const RunArgs& a, const void* W) {
     ok = make_map(&tmB, W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH);
   }
   if (!ok) return cudaErrorInvalidValue;
+  // packed scale blocks as 2-D maps: rows of 128 x 32-bit (512 bytes), SF_CELLS rows per box
+  tmSA = tmA;
+  tmSB = tmA;
+  if constexpr (C::SCALED) {
+    if (sfa && !make_map_sf(&tmSA, sfa, (uint64_t)sf_rows_a, C::SF_CELLS)) return cudaErrorInvalidValue;
+    if (sfb && !make_map_sf(&tmSB, sfb, (uint64_t)sf_rows_b, C::SF_CELLS)) return cudaErrorInvalidValue;
+  }
   TcParams p;
   p.Y = a.Y;
-  p.sfa = nullptr;
-  p.sfb = nullptr;
+  p.sfa = sfa;
+  p.sfb = sfb;
   p.N = a.N;
   p.K = a.K;
   p.M = a.M;
@@ -1268,7 +1362,7 @@ cudaError_t launch_pair(const RunArgs& a, const void* W) {
   const int cap = max_pairs[dev & 31] > 0 ? max_pairs[dev & 31] : a.num_sms / 2;
   const int pairs = tiles < cap ? tiles : cap;
   cfg.gridDim = dim3(2 * pairs);
-  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, p);
+  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, tmSA, tmSB, p);
 }
 
 template <int DT, int BN, int STAGES>
@@ -1330,6 +1424,8 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
     if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
     if (dt == kI8I8 || dt == kF8F8) return K % 16 == 0 && M % 16 == 0;
     if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;   // kind::f8f6f4 on unpacked E2M1
+    if (dt == kMX4X4) return K % 32 == 0;                  // block-scaled kinds
+    if (dt == kMX8X4 || dt == kF8X4) return K % 128 == 0;
     return false;
   }
   if (bm != 128) return false;
@@ -1405,6 +1501,30 @@ cudaError_t launch_scaled(const RunArgs& a) {
   return launch_cfg<DT, BN, STAGES>(a, W, pa, pb);
 }
 
+// Block-scaled kinds on CTA pairs (256x256 tiles): pack the scale planes into
+// per-stage blocks (one 512-byte block per 128 rows and cell), then the pair
+// kernel; each CTA brings its own rows' X scales and all 256 columns' W scales.
+template <int DT>
+cudaError_t launch_scaled_pair(const RunArgs& a) {
+  constexpr int kStagesPair = 6;
+  const ScaledWs w = scaled_ws(DT, 256, a.N, a.K, a.M);
+  if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
+  uint8_t* base = static_cast<uint8_t*>(a.ws);
+  uint8_t* pa = w.a_bytes ? base : nullptr;
+  uint8_t* pb = w.b_bytes ? base + round256(w.a_bytes) : nullptr;
+  if (pa || pb) {
+    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles};
+    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles};
+    const int tiles = w.a_tiles > w.b_tiles ? w.a_tiles : w.b_tiles;
+    const int threads = tiles * w.stages * w.cells * 32;
+    sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.cells);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pair<DT, 256, kStagesPair>(a, a.W, pa, pb, w.a_tiles * w.stages * w.cells,
+                                           w.b_tiles * w.stages * w.cells);
+}
+
 // f4f4 on CTA pairs: transpose W to [M,K] into the workspace, then
 // kind::f8f6f4 (E2M1 x E2M1) over both operands unpacked by TMA.
 cudaError_t launch_f4f4_pair(const RunArgs& a) {
@@ -1440,6 +1560,9 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
       case kI8I8: return launch_pair<kI8I8, 256, 6>(a, a.W);
       case kF8F8: return launch_pair<kF8F8, 256, 6>(a, a.W);
       case kF4F4: return launch_f4f4_pair(a);
+      case kMX4X4: return launch_scaled_pair<kMX4X4>(a);
+      case kMX8X4: return launch_scaled_pair<kMX8X4>(a);
+      case kF8X4: return launch_scaled_pair<kF8X4>(a);
       default: return cudaErrorInvalidValue;
     }
   }

@@ -255,6 +255,33 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// CTA pairs: issued by the leader, copies each CTA's own shared memory (same
+// offset) into its own TMEM (measured: the pair's A scales stay per CTA).
+__device__ __forceinline__ void tc_cp_pair_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Block-scaled MMA on a CTA pair (M = 256): each CTA's TMEM holds the scales of
+// its own 128 rows of A and of all N columns of B.
+template <int KIND>
+__device__ __forceinline__ void tc_mma_pair_bs(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate, uint32_t sfa_tmem, uint32_t sfb_tmem) {
+  if constexpr (KIND == kKindMxF8F6F4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  } else {
+    static_assert(KIND == kKindMxF4, "block-scaled kinds");
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  }
+}
+
 // Shared::cluster address of the same shared-memory location in CTA `rank`.
 __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
   uint32_t r;

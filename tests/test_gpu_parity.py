@@ -61,7 +61,7 @@ def assert_close(dtype, out, ref):
 TC_TILES = {d: ["256x256", "128x256", "128x128"] for d in ("fp16", "i8i8", "f8f8")}
 TC_TILES.update({d: ["128x256", "128x128"] for d in ("int8", "fp8", "mxfp4")})
 TC_TILES.update({"f4f4": ["256x256", "128x256", "128x128"]})
-TC_TILES.update({d: ["128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
+TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
 TC_CASES = [(d, t) for d in F.DTYPES for t in TC_TILES[d]]
 
 
