@@ -160,3 +160,13 @@ def test_stream_deterministic(gemm):
     a, ref, ops = run_case(gemm, "int8", "stream", 1, 4096, 11008)
     b, _, _ = run_case(gemm, "int8", "stream", 1, 4096, 11008, ops=ops)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "f8f8", "i8i8", "mxfp4/a8"])
+def test_pair_tiles_deterministic(gemm, dtype):
+    # CTA-pair tiles: identical bits on every call
+    N, K, M = 1000, 1024, 1296
+    a, ref, ops = run_case(gemm, dtype, "256x256", N, K, M)
+    b, _, _ = run_case(gemm, dtype, "256x256", N, K, M, ops=ops)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert_close(dtype, a, ref)
