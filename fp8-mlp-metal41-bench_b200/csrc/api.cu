@@ -64,7 +64,7 @@ const char* kKernelNames[kNumDTypes] = {"fp16_mlp_gemm", "int8_mlp_gemm", "i8i8_
                                          "f8x4_mlp_gemm"};
 
 // ---- tile table -----------------------------------------------------------------
-enum TileKind { kTileTC = 0, kTileGemv = 1, kTileStream = 2 };
+enum TileKind { kTileTC = 0, kTileGemv = 1, kTileStream = 2, kTileThin = 3 };
 struct TileDef {
   const char* name;
   TileKind kind;
@@ -73,7 +73,7 @@ struct TileDef {
 };
 const TileDef kTiles[] = {
     {"256x256", kTileTC, 256, 256},  {"128x256", kTileTC, 256, 128}, {"128x128", kTileTC, 128, 128},
-    {"stream", kTileStream, 0, 0},
+    {"16x128", kTileThin, 0, 0},     {"stream", kTileStream, 0, 0},
     {"gemv.k1", kTileGemv, 1, 0},    {"gemv.k2", kTileGemv, 2, 0},   {"gemv.k4", kTileGemv, 4, 0},
     {"gemv.k8", kTileGemv, 8, 0},    {"gemv.k16", kTileGemv, 16, 0}, {"gemv.k32", kTileGemv, 32, 0},
     {"gemv.k64", kTileGemv, 64, 0},
@@ -104,6 +104,7 @@ bool tile_ok(int dt, int t, int N, int K, int M) {
   if (!valid_tile(t) || layout_check(dt, N, K, M) != GEMM_OK) return false;
   if (kTiles[t].kind == kTileTC) return tc_supported(dt, kTiles[t].bm, kTiles[t].param, N, K, M);
   if (kTiles[t].kind == kTileStream) return stream_supported(dt, N, K, M);
+  if (kTiles[t].kind == kTileThin) return thin_supported(dt, N, K, M);
   // CUDA-core tiles: the thin-row kernel, and the fallback where no
   // tensor-core tile covers the dtype or shape.
   if (!gemv_supported(dt, kTiles[t].param, N, K, M)) return false;
@@ -149,6 +150,7 @@ int enqueue(DevState* s, int dt, int tile, const void* X, const void* W, void* Y
   cudaError_t e;
   if (kTiles[tile].kind == kTileTC) e = launch_tc(a, kTiles[tile].bm, kTiles[tile].param);
   else if (kTiles[tile].kind == kTileStream) e = launch_stream(a);
+  else if (kTiles[tile].kind == kTileThin) e = launch_thin(a);
   else e = launch_gemv(a, kTiles[tile].param);
   if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
   return GEMM_OK;
@@ -260,6 +262,10 @@ int gemm_default_tile(int dtype, int N, int K, int M) {
     if (tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
     if (tc_supported(dtype, 128, 128, N, K, M)) return gemm_tile_index("128x128");
   }
+  // 3 <= N <= 16: the tensor-core thin tile (weights as the MMA's A operand)
+  // measures 1.1-3.6x ahead of the CUDA-core kernels; at N <= 2 the split-K
+  // GEMV streams the weights faster
+  if (N >= 3 && thin_supported(dtype, N, K, M)) return gemm_tile_index("16x128");
   int sms = 148;
   for (int d = 0; d < kMaxDevices; ++d)
     if (g_dev[d].ready) { sms = g_dev[d].num_sms; break; }
@@ -273,6 +279,7 @@ size_t gemm_workspace_size(int dtype, int tile, int N, int K, int M) {
   if (!valid_tile(tile) || !valid_dtype(dtype)) return 0;
   if (kTiles[tile].kind == kTileTC) return tc_workspace(dtype, kTiles[tile].param, N, K, M);
   if (kTiles[tile].kind == kTileStream) return stream_supported(dtype, N, K, M) ? stream_workspace(dtype, N, K, M) : 0;
+  if (kTiles[tile].kind == kTileThin) return thin_workspace(dtype, N, K, M);
   return gemv_workspace(dtype, kTiles[tile].param, N, K, M);
 }
 

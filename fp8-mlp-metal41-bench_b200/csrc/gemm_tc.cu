@@ -44,6 +44,7 @@
 #include "formats.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
+#include "tmap.h"
 #include "widen.cuh"
 
 namespace mlpg {
@@ -1115,6 +1116,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
   }
 }
 
+}  // namespace
+
 // ----------------------------------------------------------------------------
 // host side: tensor maps through the driver entry point (no libcuda link)
 // ----------------------------------------------------------------------------
@@ -1178,6 +1181,8 @@ bool make_map_sf(CUtensorMap* m, const void* base, uint64_t rows, uint32_t cells
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+namespace {
 
 int current_device() {
   int d = 0;

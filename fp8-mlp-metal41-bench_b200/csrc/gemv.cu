@@ -25,6 +25,7 @@
 
 #include "formats.cuh"
 #include "kernels.h"
+#include "partition.cuh"
 #include "ptx.cuh"
 
 namespace mlpg {
@@ -53,20 +54,6 @@ struct GemvParams {
   int units_per_slab;
   int total_units;
 };
-
-// contiguous unit range of CTA c of G (stream-K)
-__device__ __forceinline__ void cta_range(int c, int G, int U, int& u0, int& u1) {
-  u0 = (int)((long long)c * U / G);
-  u1 = (int)((long long)(c + 1) * U / G);
-}
-
-// first CTA whose range contains unit u
-__device__ __forceinline__ int owner_of(int u, int G, int U) {
-  int c = (int)(((long long)u * G + G - 1) / U);   // largest c with c*U/G <= u
-  while (c > 0 && (long long)c * U / G > u) --c;
-  while ((long long)(c + 1) * U / G <= u) ++c;
-  return c;
-}
 
 // Bytes per weight element, times two (FP4 packs two per byte).
 template <int DT>

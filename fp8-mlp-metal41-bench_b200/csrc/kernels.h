@@ -35,6 +35,13 @@ bool stream_supported(int dt, int N, int K, int M);
 size_t stream_workspace(int dt, int N, int K, int M);
 cudaError_t launch_stream(const RunArgs& a);
 
+// ---- thin rows on the tensor cores (N <= 16; weights as the MMA's A operand) ----
+// Stream-K over (128-row weight tile, K stage) units, one CTA per SM; shared
+// tiles are summed through the workspace (counters zero before first use).
+bool thin_supported(int dt, int N, int K, int M);
+size_t thin_workspace(int dt, int N, int K, int M);
+cudaError_t launch_thin(const RunArgs& a);
+
 // ---- tcgen05 tensor-core GEMM --------------------------------------------------
 // bm: 128 (one CTA per tile) or 256 (a CTA pair, cta_group::2); bn: 128 or 256.
 bool tc_supported(int dt, int bm, int bn, int N, int K, int M);

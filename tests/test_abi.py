@@ -58,6 +58,15 @@ def test_layout_rules_and_tile_support():
     # thin rows: the CUDA-core kernel; the default tile is a gemv tile
     assert G.tile_names()[G.default_tile(F.CODE["int8"], 1, 4096, 11008)].startswith("gemv")
     assert G.tile_names()[G.default_tile(F.CODE["i8i8"], 4096, 4096, 4096)] == "256x256"
+    # 3 <= N <= 16: the tensor-core thin tile where it covers the dtype
+    for d in ("fp16", "int8", "i8i8", "fp8", "f8f8", "mxfp4"):
+        assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "16x128"
+    assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 8, 4096, 11008)].startswith("gemv")
+    t16 = G.tile_index("16x128")
+    assert G.tile_supported(F.CODE["fp16"], t16, 16, 4096, 11008)
+    assert not G.tile_supported(F.CODE["fp16"], t16, 17, 4096, 11008)     # N <= 16
+    assert not G.tile_supported(F.CODE["i8i8"], t16, 4, 4104, 11008)      # byte X: K % 16
+    assert not G.tile_supported(F.CODE["mxfp4/a8"], t16, 4, 4096, 11008)  # no thin kernel for this kind
 
 
 def test_workspace_sizes():

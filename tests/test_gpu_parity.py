@@ -162,6 +162,78 @@ def test_stream_deterministic(gemm):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+# thin rows on the tensor cores: weights as the MMA's A operand (tile 16x128)
+THIN_TC = ["fp16", "int8", "i8i8", "fp8", "f8f8", "mxfp4"]
+
+
+def thin_k(dtype, K):
+    # the tile's TMA strides: K % 8 for half X, % 16 for byte X, % 32 for MX weights
+    step = 32 if dtype in F.W_MX else (16 if dtype in ("i8i8", "f8f8") else 8)
+    return max(step, K // step * step)
+
+
+@pytest.mark.parametrize("dtype", THIN_TC)
+@pytest.mark.parametrize("shape", [(1, 4096, 11008), (1, 1024, 1504), (3, 1000, 1296), (16, 512, 640),
+                                   (5, 64, 128), (2, 8192, 256), (7, 200, 4096)])
+def test_thin_tensor_core_tile(gemm, dtype, shape):
+    # stream-K over (tile, K stage) units: whole tiles, tiles shared by many
+    # CTAs (K=8192, two tiles), a single unit, ragged K and ragged M
+    N, K, M = shape
+    K = thin_k(dtype, K)
+    out, ref, _ = run_case(gemm, dtype, "16x128", N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", THIN_TC)
+def test_thin_tensor_core_reference_patterns(gemm, dtype):
+    out, ref, _ = run_case(gemm, dtype, "16x128", 4, 1024, 768, mode="ref")
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("lo,hi", [(124, 130), (90, 100), (150, 160), (100, 145), (40, 214)])
+def test_thin_mxfp4_any_scale_range(gemm, lo, hi):
+    # per-(CTA, row) exponent offsets keep the widened weights exact in f16
+    # (the widest range keeps the f32 results finite: 2^(214-127) * 6 * |x| * K)
+    N, K, M = 3, 2048, 384
+    ops = Operands(N, K, M, "seeded", 4)
+    rng = np.random.default_rng(11)
+    ops._cache["wscale"] = rng.integers(lo, hi + 1, M * (K // 32), dtype=np.uint8)
+    out, ref, _ = run_case(gemm, "mxfp4", "16x128", N, K, M, ops=ops)
+    if hi - lo <= 36:
+        assert_close("mxfp4", out, ref)
+    else:
+        # a row whose scales span more than f16's range loses only terms
+        # below 2^-24 of its largest block
+        rms = float(np.sqrt(np.mean(ref * ref)))
+        assert np.all(np.abs(out - ref) <= 1e-3 * np.maximum(np.abs(ref), 1e-2 * rms))
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "i8i8", "mxfp4"])
+def test_thin_tensor_core_deterministic(gemm, dtype):
+    # two calls on ONE workspace: identical bits (shared tiles are summed in
+    # CTA order) and the tile counters are back at zero for the second call
+    G = gemm
+    N, K, M = 2, 4096, 11008
+    ops = Operands(N, K, M, "seeded", 3)
+    dt, ti = F.CODE[dtype], G.tile_index("16x128")
+    bufs = [G.DeviceBuffer(0, a.nbytes).upload(a) for a in (ops.X(dtype), ops.W(dtype))]
+    ws = ops.wscale(dtype)
+    WS = G.DeviceBuffer(0, ws.nbytes).upload(ws) if ws is not None else None
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero()
+    outs = []
+    for _ in range(2):
+        Y = G.DeviceBuffer(0, N * M * 4).zero()
+        G.run(0, dt, ti, bufs[0], bufs[1], Y, N, K, M, None, WS, WSP, wsb)
+        G.sync(0)
+        o = np.empty((N, M), dtype=np.int32 if dtype == "i8i8" else np.float32)
+        Y.download(o)
+        outs.append(o)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), None, ws, N, K, M)
+    assert_close(dtype, outs[1], ref)
+
+
 @pytest.mark.parametrize("dtype", ["fp16", "f8f8", "i8i8", "mxfp4/a8"])
 def test_pair_tiles_deterministic(gemm, dtype):
     # CTA-pair tiles: identical bits on every call
