@@ -112,13 +112,23 @@ struct ThinCfg {
   static constexpr int RAW_BYTES = W_BYTES + X_BOXES * X_BOX;    // 18 / 20 / 24 KB
   static constexpr int RAW_STAGES = STAGES;
   static constexpr int CV_STAGES = DIRECT ? 0 : 3;
-  static constexpr int CV_BYTES = kTBM * CV_K * 2;               // 128 rows x 128 f16 of K
+  // mxfp4 rows are K-major, one row per converter thread: the widened rows go
+  // straight to TMEM (the MMA's A operand may sit there), which keeps the
+  // 4x-expanded f16 stream out of shared memory.  The [K,M] bytes need a
+  // transpose to become TMEM rows, so int8 / fp8 widen into shared memory.
+  static constexpr bool A_TMEM = MX;
+  static constexpr int CV_A_BYTES = A_TMEM ? 0 : kTBM * CV_K * 2;   // 128 rows x 128 f16 of K
+  // a converted slot holds its A tile (shared-memory kinds) and a copy of its
+  // two X boxes, so that a raw slot is free again as soon as it is converted
+  static constexpr int CV_SLOT = CV_A_BYTES + 2 * X_BOX;
+  static constexpr int A_COL0 = 2 * kTBN;                        // TMEM: after the two accumulators
+  static constexpr int A_COLS = CV_K / 2;                        // TMEM columns per converted stage
+  static constexpr uint32_t TMEM_COLS = A_TMEM ? 256u : 32u;
   static constexpr int CV_OFF = RAW_STAGES * RAW_BYTES;
-  static constexpr int OFFS_OFF = CV_OFF + CV_STAGES * CV_BYTES;  // mxfp4: 2 x 128 exponent offsets
+  static constexpr int OFFS_OFF = CV_OFF + CV_STAGES * CV_SLOT;   // mxfp4: 2 x 128 exponent offsets
   static constexpr int BAR_OFF = OFFS_OFF + (MX ? 2 * kTBM * 4 : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;        // + barriers + alignment slack
   static constexpr int MMAS = DIRECT ? 4 : 8;                     // per (sub-)stage, 32 bytes of K each
-  static constexpr int B_BOXES_PER_SUB = DIRECT ? 1 : 2;          // X boxes (4 MMAs each) per (sub-)stage
   // A (weights): MN-major for the [K,M] layouts -- two 64-column halves
   // (8 KB apart from TMA, 16 KB apart when converted) for 16-bit elements,
   // one 128-column atom for 8-bit -- and K-major for the widened mxfp4 rows
@@ -133,15 +143,16 @@ struct ThinCfg {
   static constexpr uint32_t IDESC = (T::cfmt << 4) | (T::fmt << 7) | (T::fmt << 10) |
                                     ((A_MN ? 1u : 0u) << 15) | ((uint32_t)(kTBN >> 3) << 17) |
                                     ((uint32_t)(kTBM >> 4) << 24);
-  static_assert(RAW_BYTES % 1024 == 0 && CV_BYTES % 1024 == 0, "swizzle atoms need 1 KB alignment");
+  static_assert(RAW_BYTES % 1024 == 0 && CV_SLOT % 1024 == 0, "swizzle atoms need 1 KB alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
   static_assert(STAGES <= 10, "barrier array");
+  static_assert(!A_TMEM || A_COL0 + CV_STAGES * A_COLS <= (int)TMEM_COLS, "TMEM budget");
 };
 
 // default ring depth: as deep as shared memory allows
 template <int DT>
 constexpr int thin_stages() {
-  return ThinT<DT>::mode == kThinDirect ? 10 : 4;
+  return ThinT<DT>::mode == kThinDirect ? 10 : (ThinT<DT>::mode == kThinWidenMX ? 8 : 5);
 }
 
 struct ThinBars {
@@ -198,8 +209,8 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::RAW_STAGES; ++s) {
       mbar_init(&bars->raw_full[s], 1);
-      // released by the MMAs (X and, for direct kinds, W) and by every converter warp (W)
-      mbar_init(&bars->raw_empty[s], C::DIRECT ? 1 : 1 + kConvWarps);
+      // released by the MMAs (direct kinds) or by every converter warp
+      mbar_init(&bars->raw_empty[s], C::DIRECT ? 1 : kConvWarps);
     }
     for (int s = 0; s < C::CV_STAGES; ++s) {
       mbar_init(&bars->cv_full[s], kConvWarps);
@@ -217,7 +228,7 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, 32);
+    tmem_alloc(&bars->tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -278,25 +289,35 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
         if (!mbar_wait(&bars->acc_empty[buf], ((uint32_t)(seg >> 1) & 1u) ^ 1u, ctl, 0x200 + buf)) break;
         tc_fence_after();
       }
-      if (!mbar_wait(&bars->raw_full[rs], rph, ctl, 0x300 + rs)) break;
-      tc_fence_after();
+      if constexpr (C::DIRECT) {
+        // converted kinds read only converted slots (cv_full); their raw slots
+        // are recycled by the converters and may run ahead of this thread
+        if (!mbar_wait(&bars->raw_full[rs], rph, ctl, 0x300 + rs)) break;
+        tc_fence_after();
+      }
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kTBN);
       const uint32_t w_addr = sbase + rs * C::RAW_BYTES;
 #pragma unroll 1
       for (int sub = 0; sub < C::SUBS; ++sub) {
-        uint32_t a_addr = w_addr;
+        uint32_t a_addr = w_addr, b_addr = w_addr + C::W_BYTES;
         if constexpr (!C::DIRECT) {
           if (!mbar_wait(&bars->cv_full[cs], cph, ctl, 0x500 + cs)) { ok = false; break; }
           tc_fence_after();
-          a_addr = sbase + C::CV_OFF + cs * C::CV_BYTES;
+          a_addr = sbase + C::CV_OFF + cs * C::CV_SLOT;
+          b_addr = a_addr + C::CV_A_BYTES;
         }
-        const uint32_t b_addr = w_addr + C::W_BYTES + sub * C::B_BOXES_PER_SUB * C::X_BOX;
 #pragma unroll
         for (int kk = 0; kk < C::MMAS; ++kk) {
-          const uint64_t ad = sdesc_sw128(
-              a_addr + (kk / C::A_GRP) * C::A_GRP_STRIDE + (kk % C::A_GRP) * C::A_STEP, C::A_LBO, 1024);
           const uint64_t bd = sdesc_sw128(b_addr + (kk / 4) * C::X_BOX + (kk % 4) * 32, 16, 1024);
-          tc_mma<T::kind>(d_tmem, ad, bd, C::IDESC, (first && sub == 0 && kk == 0) ? 0u : 1u);
+          const uint32_t acc = (first && sub == 0 && kk == 0) ? 0u : 1u;
+          if constexpr (C::A_TMEM) {
+            // K = 16 per MMA: 8 TMEM columns of the converted stage
+            tc_mma_f16_ta(d_tmem, tmem_base + (uint32_t)(C::A_COL0 + cs * C::A_COLS + kk * 8), bd, C::IDESC, acc);
+          } else {
+            const uint64_t ad = sdesc_sw128(
+                a_addr + (kk / C::A_GRP) * C::A_GRP_STRIDE + (kk % C::A_GRP) * C::A_STEP, C::A_LBO, 1024);
+            tc_mma<T::kind>(d_tmem, ad, bd, C::IDESC, acc);
+          }
         }
         if constexpr (!C::DIRECT) {
           tc_commit(&bars->cv_empty[cs]);
@@ -304,8 +325,10 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
         }
       }
       if (!ok) break;
-      tc_commit(&bars->raw_empty[rs]);
-      if (++rs == C::RAW_STAGES) { rs = 0; rph ^= 1u; }
+      if constexpr (C::DIRECT) {
+        tc_commit(&bars->raw_empty[rs]);
+        if (++rs == C::RAW_STAGES) { rs = 0; rph ^= 1u; }
+      }
       if (last) {
         tc_commit(&bars->acc_full[buf]);
         ++seg;
@@ -394,19 +417,32 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
 #pragma unroll 1
         for (int sub = 0; sub < C::SUBS; ++sub) {
           if (!mbar_wait_warp(&bars->cv_empty[cs], cph ^ 1u, ctl, 0xA00 + cs)) { ok = false; break; }
-          unsigned char* cv = smem + C::CV_OFF + cs * C::CV_BYTES;
+          unsigned char* cv = smem + C::CV_OFF + cs * C::CV_SLOT;
+          // this stage's two X boxes (4 KB, already in the MMA's layout): 8 bytes per thread
+          *reinterpret_cast<uint2*>(cv + C::CV_A_BYTES + ct * 8) =
+              *reinterpret_cast<const uint2*>(raw + C::W_BYTES + sub * 2 * C::X_BOX + ct * 8);
           if constexpr (C::MX) {
             // raw rows of 128 B (128-byte swizzle): k-block blk of row r is chunk
-            // blk ^ (r & 7); its 32 E2M1 -> four f16 chunks of the K-major row,
-            // in K atom bq / 2 (16 KB apart), chunks 4 * (bq & 1) .. + 3
+            // blk ^ (r & 7); its 32 E2M1 -> 16 TMEM columns (two f16 of K each) of
+            // lane r, columns 16 * bq .. of the converted stage.  Warp w reaches
+            // the TMEM lanes of quadrant w % 4, which holds rows r = 32 * (w % 4) + lane.
             const int blk = 4 * sub + bq;
             const uint4 w = *reinterpret_cast<const uint4*>(raw + r * kTRow + ((blk ^ (r & 7)) << 4));
             const uint32_t mul = f16x2_pow2(sc[sub] - 127 - c_row);
-            unsigned char* row = cv + (bq >> 1) * (kTBM * kTRow) + r * kTRow;
             const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+            uint32_t h[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              *reinterpret_cast<uint4*>(row + (((4 * (bq & 1) + i) ^ (r & 7)) << 4)) = widen_e2m1x8(words[i], mul);
+            for (int i = 0; i < 4; ++i) {
+              const uint4 t = widen_e2m1x8(words[i], mul);
+              h[4 * i] = t.x;
+              h[4 * i + 1] = t.y;
+              h[4 * i + 2] = t.z;
+              h[4 * i + 3] = t.w;
+            }
+            tmem_st_32x32b_x16(tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) +
+                                   (uint32_t)(C::A_COL0 + cs * C::A_COLS + 16 * bq),
+                               h);
+            tmem_st_wait();
           } else {
             // raw [128 K rows][128 B of M] -> two MN-major halves [128 K rows][64
             // columns of f16], 16 KB apart, 128-byte swizzle
@@ -421,6 +457,7 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
             }
           }
           fence_proxy_async_smem();   // generic-proxy writes -> visible to tcgen05.mma
+          if constexpr (C::A_TMEM) tc_fence_before();   // tcgen05.st -> the MMA thread
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->cv_full[cs]);
           if (++cs == C::CV_STAGES) { cs = 0; cph ^= 1u; }
@@ -513,7 +550,7 @@ __global__ void __launch_bounds__(ThinCfg<DT, STAGES>::THREADS, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, 32);
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
