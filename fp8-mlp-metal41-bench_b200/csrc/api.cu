@@ -258,7 +258,10 @@ int gemm_default_tile(int dtype, int N, int K, int M) {
     // (which keeps one accumulator in TMEM next to its scale cells)
     const bool scaled = dtype == kMX4X4 || dtype == kMX8X4 || dtype == kF8X4;
     if (scaled && tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
-    if (tc_supported(dtype, 256, 256, N, K, M)) return gemm_tile_index("256x256");
+    // A16 kinds on the pair tile widen all of W to f16 first: worth it once the
+    // per-128-row conversions of the 1-CTA tiles would repeat (N >= 256)
+    const bool a16 = dtype == kINT8 || dtype == kFP8 || dtype == kMXFP4;
+    if ((!a16 || N >= 256) && tc_supported(dtype, 256, 256, N, K, M)) return gemm_tile_index("256x256");
     if (tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
     if (tc_supported(dtype, 128, 128, N, K, M)) return gemm_tile_index("128x128");
   }
@@ -277,7 +280,7 @@ int gemm_default_tile(int dtype, int N, int K, int M) {
 
 size_t gemm_workspace_size(int dtype, int tile, int N, int K, int M) {
   if (!valid_tile(tile) || !valid_dtype(dtype)) return 0;
-  if (kTiles[tile].kind == kTileTC) return tc_workspace(dtype, kTiles[tile].param, N, K, M);
+  if (kTiles[tile].kind == kTileTC) return tc_workspace(dtype, kTiles[tile].bm, kTiles[tile].param, N, K, M);
   if (kTiles[tile].kind == kTileStream) return stream_supported(dtype, N, K, M) ? stream_workspace(dtype, N, K, M) : 0;
   if (kTiles[tile].kind == kTileThin) return thin_workspace(dtype, N, K, M);
   return gemv_workspace(dtype, kTiles[tile].param, N, K, M);
@@ -286,7 +289,7 @@ size_t gemm_workspace_size(int dtype, int tile, int N, int K, int M) {
 int gemm_launches_per_run(int dtype, int tile, int N, int K, int M) {
   (void)N; (void)K; (void)M;
   if (!valid_tile(tile)) return 0;
-  return kTiles[tile].kind == kTileTC ? tc_launches(dtype) : 1;
+  return kTiles[tile].kind == kTileTC ? tc_launches(dtype, kTiles[tile].bm) : 1;
 }
 
 void* gemm_alloc(int device, size_t bytes) {

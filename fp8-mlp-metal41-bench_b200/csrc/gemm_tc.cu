@@ -68,6 +68,8 @@ struct Traits;
 // operands K-major (W transposed to [M,K] first) and unpacked by TMA into
 // 8-bit containers in shared memory (16U4_ALIGN16B).
 constexpr int kF4F4Pair = 64;
+// mxfp4 weights widened to f16 in their own [M,K] layout: kind::f16 with B K-major
+constexpr int kF16K = 65;
 
 template <>
 struct Traits<kFP16> {
@@ -112,6 +114,12 @@ struct Traits<kF4F4Pair> {
   static constexpr uint32_t a_fmt = 5, b_fmt = 5, c_fmt = 1;  // E2M1, E2M1 -> F32
 };
 template <>
+struct Traits<kF16K> {
+  static constexpr int kind = kKindF16, a_bits = 16, b_bits = 16, nsf = 0;
+  static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = false;
+  static constexpr uint32_t a_fmt = 0, b_fmt = 0, c_fmt = 1;  // F16, F16 -> F32
+};
+template <>
 struct Traits<kF8X4> {
   static constexpr int kind = kKindMxF8F6F4, a_bits = 8, b_bits = 8, nsf = 1;
   static constexpr bool b_mn = false, x_plane = false, w_plane = true, b_unpack4 = true;
@@ -122,6 +130,7 @@ struct TcParams {
   void* Y;
   const uint8_t* sfa;      // packed X scale blocks (see sf_pack_kernel) or null (scale 1)
   const uint8_t* sfb;      // packed W scale blocks or null (scale 1)
+  const int8_t* col_exp;   // per output column: Y *= 2^col_exp (exact), or null
   int N, K, M;
   int tiles_m, tiles_n, num_kb;
   int* dev_err;
@@ -254,11 +263,18 @@ __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb
 // being stored.
 template <int NCH, typename Release>
 __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, int col0, int M, bool row_ok,
-                                               Release release) {
+                                               const int8_t* col_exp, Release release) {
   const bool vec_ok = (M % 4) == 0;
-  auto store = [&](const uint32_t (&r)[32], int c) {
+  auto store = [&](uint32_t (&r)[32], int c) {
     const int cb = col0 + c * 32;
     if (!row_ok) return;
+    if (col_exp) {   // f32 results times 2^e per column (exact powers of two)
+#pragma unroll
+      for (int v = 0; v < 32; ++v) {
+        const int e = cb + v < M ? col_exp[cb + v] : 0;
+        if (e) r[v] = __float_as_uint(__uint_as_float(r[v]) * __int_as_float((e + 127) << 23));
+      }
+    }
     if (vec_ok && cb + 32 <= M) {
       uint4* dst = reinterpret_cast<uint4*>(yrow + cb);
 #pragma unroll
@@ -471,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_COLS), yrow, col0,
-                              p.M, row_ok, [&] {
+                              p.M, row_ok, p.col_exp, [&] {
                                 tc_fence_before();
                                 mbar_arrive(&bars->acc_empty[buf]);
                               });
@@ -786,7 +802,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN), yrow, col0, p.M,
-                              row_ok, [&] {
+                              row_ok, p.col_exp, [&] {
                                 tc_fence_before();
                                 __syncwarp();
                                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
@@ -1116,6 +1132,63 @@ __global__ void __launch_bounds__(kWThreads, 1)
   }
 }
 
+// ----------------------------------------------------------------------------
+// A16 kinds on CTA pairs: the [K,M] int8 / E4M3 weights are widened once per
+// call to f16 in the workspace (exact), and the fp16 pair kernel runs on them.
+// At the fat shape the widening (one read of W, one write of twice its bytes)
+// costs about a tenth of the GEMM, whereas the converter warps of the widen
+// kernel redo it for every 128 rows of X.
+// ----------------------------------------------------------------------------
+template <int DT>
+__global__ void __launch_bounds__(256) widen_w_f16_kernel(const uint8_t* __restrict__ W, uint4* __restrict__ out,
+                                                          long n16) {
+  for (long i = blockIdx.x * 256L + threadIdx.x; i < n16; i += (long)gridDim.x * 256L) {
+    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(W) + i);   // 16 weights, read once
+    const uint2 lo = make_uint2(v.x, v.y), hi = make_uint2(v.z, v.w);
+    out[2 * i] = DT == kINT8 ? widen_i8x8(lo) : widen_e4m3x8(lo);
+    out[2 * i + 1] = DT == kINT8 ? widen_i8x8(hi) : widen_e4m3x8(hi);
+  }
+}
+
+// mxfp4 weights [M,K] (E2M1, UE8M0 per 32) widened once to f16 [M,K], one warp
+// per weight row: the row's exponent offset c_m (the rule of mx_row_exp_kernel)
+// keeps E2M1 * 2^(s-127-c_m) exact in f16, and col_exp[m] = c_m tells the GEMM
+// epilogue to multiply output column m by 2^c_m.
+__global__ void __launch_bounds__(256) widen_mx_f16_kernel(const uint8_t* __restrict__ W,
+                                                           const uint8_t* __restrict__ wscale, int M, int K,
+                                                           uint4* __restrict__ out, int8_t* __restrict__ col_exp) {
+  const int m = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (m >= M) return;   // warp-uniform
+  const int kbpr = K / 32;
+  const uint8_t* srow = wscale + (size_t)m * kbpr;
+  int mn = 255, mx = 0;
+  for (int i = lane; i < kbpr; i += 32) {
+    const int sc = __ldg(srow + i);
+    mn = min(mn, sc);
+    mx = max(mx, sc);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  int c = 0;
+  if (mx > 140) c = mx - 140;
+  else if (mn < 104) c = max(mn - 104, mx - 140);
+  if (lane == 0) col_exp[m] = (int8_t)c;
+  // one 16-byte block (32 E2M1, one scale) per lane and step -> 64 bytes of f16
+  const uint4* wrow = reinterpret_cast<const uint4*>(W + (size_t)m * (K / 2));
+  uint4* orow = out + (size_t)m * (K / 8);
+  for (int b = lane; b < kbpr; b += 32) {
+    const uint4 w = __ldcs(wrow + b);
+    const uint32_t mul = f16x2_pow2((int)__ldg(srow + b) - 127 - c);
+    orow[4 * b] = widen_e2m1x8(w.x, mul);
+    orow[4 * b + 1] = widen_e2m1x8(w.y, mul);
+    orow[4 * b + 2] = widen_e2m1x8(w.z, mul);
+    orow[4 * b + 3] = widen_e2m1x8(w.w, mul);
+  }
+}
+
 }  // namespace
 
 // ----------------------------------------------------------------------------
@@ -1224,6 +1297,7 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   p.Y = a.Y;
   p.sfa = sfa;
   p.sfb = sfb;
+  p.col_exp = nullptr;
   p.N = a.N;
   p.K = a.K;
   p.M = a.M;
@@ -1247,7 +1321,7 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
 
 template <int DT, int BN, int STAGES>
 cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nullptr, const uint8_t* sfb = nullptr,
-                        int sf_rows_a = 0, int sf_rows_b = 0) {
+                        int sf_rows_a = 0, int sf_rows_b = 0, const int8_t* col_exp = nullptr) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
   CUtensorMap tmA, tmB, tmSA, tmSB;
@@ -1288,6 +1362,7 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   p.Y = a.Y;
   p.sfa = sfa;
   p.sfb = sfb;
+  p.col_exp = col_exp;
   p.N = a.N;
   p.K = a.K;
   p.M = a.M;
@@ -1383,6 +1458,8 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
   if (bm == 256) {   // CTA-pair tiles: the unscaled kinds, 256-wide
     if (bn != 256) return false;
     if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
+    if (dt == kINT8 || dt == kFP8) return K % 8 == 0 && M % 16 == 0;   // widened to f16 first
+    if (dt == kMXFP4) return K % 32 == 0;                               // widened to f16 [M,K] first
     if (dt == kI8I8 || dt == kF8F8) return K % 16 == 0 && M % 16 == 0;
     if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;   // kind::f8f6f4 on unpacked E2M1
     if (dt == kMX4X4) return K % 32 == 0;                  // block-scaled kinds
@@ -1501,16 +1578,49 @@ cudaError_t launch_f4f4_pair(const RunArgs& a) {
 
 }  // namespace
 
-size_t tc_workspace(int dt, int bn, int N, int K, int M) {
+size_t tc_workspace(int dt, int bm, int bn, int N, int K, int M) {
   if (is_scaled(dt)) return scaled_ws(dt, bn, N, K, M).total();
+  if (bm == 256 && (dt == kINT8 || dt == kFP8)) return round256((size_t)K * M * 2);   // f16 copy of W
+  if (bm == 256 && dt == kMXFP4) return round256((size_t)K * M * 2) + round256((size_t)M);   // + column offsets
   if (dt == kMXFP4) return (size_t)M + 256;          // per-row exponent offsets
   return 0;
 }
 
-int tc_launches(int dt) {
+int tc_launches(int dt, int bm) {
   if (dt == kMXFP4 || dt == kF4F4 || dt == kMX4X4 || dt == kMX8X4 || dt == kF8X4) return 2;
+  if (bm == 256 && (dt == kINT8 || dt == kFP8)) return 2;
   return 1;
 }
+
+namespace {
+
+template <int DT>
+cudaError_t launch_widened_pair(const RunArgs& a) {
+  const size_t need = (size_t)a.K * a.M * 2;
+  if (!a.ws || a.ws_bytes < need || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
+  const long n16 = (long)a.K * a.M / 16;   // M % 16 == 0
+  long g = (n16 + 255) / 256;
+  if (g > 8L * a.num_sms) g = 8L * a.num_sms;
+  widen_w_f16_kernel<DT><<<(unsigned)g, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W),
+                                                           static_cast<uint4*>(a.ws), n16);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_pair<kFP16, 256, 6>(a, a.ws);
+}
+
+cudaError_t launch_widened_mx_pair(const RunArgs& a) {
+  const size_t wbytes = round256((size_t)a.K * a.M * 2);
+  if (!a.ws || a.ws_bytes < wbytes + round256((size_t)a.M) || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
+  uint4* w16 = static_cast<uint4*>(a.ws);
+  int8_t* col_exp = static_cast<int8_t*>(a.ws) + wbytes;
+  widen_mx_f16_kernel<<<(a.M + 7) / 8, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), a.wscale, a.M, a.K,
+                                                           w16, col_exp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_pair<kF16K, 256, 6>(a, w16, nullptr, nullptr, 0, 0, col_exp);
+}
+
+}  // namespace
 
 cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
   if (!tc_supported(a.dt, bm, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
@@ -1520,6 +1630,9 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
       case kFP16: return launch_pair<kFP16, 256, 6>(a, a.W);
       case kI8I8: return launch_pair<kI8I8, 256, 6>(a, a.W);
       case kF8F8: return launch_pair<kF8F8, 256, 6>(a, a.W);
+      case kINT8: return launch_widened_pair<kINT8>(a);
+      case kFP8: return launch_widened_pair<kFP8>(a);
+      case kMXFP4: return launch_widened_mx_pair(a);
       case kF4F4: return launch_f4f4_pair(a);
       case kMX4X4: return launch_scaled_pair<kMX4X4>(a);
       case kMX8X4: return launch_scaled_pair<kMX8X4>(a);
@@ -1534,7 +1647,7 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
     case kINT8: return bn == 256 ? launch_widen<kINT8, 256, 3>(a) : launch_widen<kINT8, 128, 5>(a);
     case kFP8: return bn == 256 ? launch_widen<kFP8, 256, 3>(a) : launch_widen<kFP8, 128, 5>(a);
     case kMXFP4: {
-      if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+      if (!a.ws || a.ws_bytes < tc_workspace(a.dt, bm, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
       return bn == 256 ? launch_widen<kMXFP4, 256, 3>(a) : launch_widen<kMXFP4, 128, 5>(a);
     }
     case kMX4X4: return bn == 256 ? launch_scaled<kMX4X4, 256, 4>(a) : launch_scaled<kMX4X4, 128, 5>(a);

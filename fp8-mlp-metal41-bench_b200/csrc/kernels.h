@@ -45,8 +45,8 @@ cudaError_t launch_thin(const RunArgs& a);
 // ---- tcgen05 tensor-core GEMM --------------------------------------------------
 // bm: 128 (one CTA per tile) or 256 (a CTA pair, cta_group::2); bn: 128 or 256.
 bool tc_supported(int dt, int bm, int bn, int N, int K, int M);
-size_t tc_workspace(int dt, int bn, int N, int K, int M);
-int tc_launches(int dt);
+size_t tc_workspace(int dt, int bm, int bn, int N, int K, int M);
+int tc_launches(int dt, int bm);
 cudaError_t launch_tc(const RunArgs& a, int bm, int bn);
 
 // Read `bytes` of `buf` (a buffer larger than L2) so that L2 holds only clean

@@ -58,6 +58,11 @@ def test_layout_rules_and_tile_support():
     # thin rows: the CUDA-core kernel; the default tile is a gemv tile
     assert G.tile_names()[G.default_tile(F.CODE["int8"], 1, 4096, 11008)].startswith("gemv")
     assert G.tile_names()[G.default_tile(F.CODE["i8i8"], 4096, 4096, 4096)] == "256x256"
+    # A16 kinds: W widened once to f16 for the CTA pair from N = 256 on
+    for d in ("int8", "fp8", "mxfp4"):
+        assert G.tile_names()[G.default_tile(F.CODE[d], 2048, 4096, 11008)] == "256x256"
+        assert G.tile_names()[G.default_tile(F.CODE[d], 128, 4096, 11008)] == "128x256"
+        assert G.workspace_size(F.CODE[d], G.tile_index("256x256"), 2048, 4096, 11008) >= 2 * 4096 * 11008
     # 3 <= N <= 16: the tensor-core thin tile where it covers the dtype
     for d in ("fp16", "int8", "i8i8", "fp8", "f8f8", "mxfp4"):
         assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "16x128"

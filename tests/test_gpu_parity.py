@@ -59,7 +59,8 @@ def assert_close(dtype, out, ref):
 
 # tensor-core tiles per dtype
 TC_TILES = {d: ["256x256", "128x256", "128x128"] for d in ("fp16", "i8i8", "f8f8")}
-TC_TILES.update({d: ["128x256", "128x128"] for d in ("int8", "fp8", "mxfp4")})
+TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("int8", "fp8")})   # 256x256: W widened once
+TC_TILES.update({"mxfp4": ["256x256", "128x256", "128x128"]})   # 256x256: widened once, K-major f16
 TC_TILES.update({"f4f4": ["256x256", "128x256", "128x128"]})
 TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
 TC_CASES = [(d, t) for d in F.DTYPES for t in TC_TILES[d]]
@@ -81,15 +82,16 @@ def test_tensor_core_reference_patterns(gemm, dtype):
     assert_close(dtype, out, ref)
 
 
+@pytest.mark.parametrize("tile", ["256x256", "128x256"])
 @pytest.mark.parametrize("lo,hi", [(124, 130), (90, 100), (150, 160), (100, 145)])
-def test_mxfp4_widen_any_scale_range(gemm, lo, hi):
+def test_mxfp4_widen_any_scale_range(gemm, lo, hi, tile):
     # E2M1 * 2^(s-127) leaves the f16 range outside s in [104, 140]; the
     # per-row exponent offsets keep the widened weights exact
     N, K, M = 256, 512, 384
     ops = Operands(N, K, M, "seeded", 4)
     rng = np.random.default_rng(9)
     ops._cache["wscale"] = rng.integers(lo, hi + 1, M * (K // 32), dtype=np.uint8)
-    out, ref, _ = run_case(gemm, "mxfp4", "128x256", N, K, M, ops=ops)
+    out, ref, _ = run_case(gemm, "mxfp4", tile, N, K, M, ops=ops)
     if hi - lo <= 36:
         assert_close("mxfp4", out, ref)
     else:
