@@ -68,8 +68,6 @@ struct Traits;
 // operands K-major (W transposed to [M,K] first) and unpacked by TMA into
 // 8-bit containers in shared memory (16U4_ALIGN16B).
 constexpr int kF4F4Pair = 64;
-// mxfp4 weights widened to f16 in their own [M,K] layout: kind::f16 with B K-major
-constexpr int kF16K = 65;
 
 template <>
 struct Traits<kFP16> {
@@ -112,12 +110,6 @@ struct Traits<kF4F4Pair> {
   static constexpr int kind = kKindF8F6F4, a_bits = 8, b_bits = 8, nsf = 0;
   static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = true;
   static constexpr uint32_t a_fmt = 5, b_fmt = 5, c_fmt = 1;  // E2M1, E2M1 -> F32
-};
-template <>
-struct Traits<kF16K> {
-  static constexpr int kind = kKindF16, a_bits = 16, b_bits = 16, nsf = 0;
-  static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = false;
-  static constexpr uint32_t a_fmt = 0, b_fmt = 0, c_fmt = 1;  // F16, F16 -> F32
 };
 template <>
 struct Traits<kF8X4> {
@@ -269,10 +261,28 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
     const int cb = col0 + c * 32;
     if (!row_ok) return;
     if (col_exp) {   // f32 results times 2^e per column (exact powers of two)
+      // the chunk's 32 exponents in two 16-byte loads (the same for every lane);
+      // nothing to do when all are zero, the usual case
+      uint32_t e4[8];
+      if (cb + 32 <= M) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(col_exp + cb));
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(col_exp + cb + 16));
+        e4[0] = a.x, e4[1] = a.y, e4[2] = a.z, e4[3] = a.w, e4[4] = b.x, e4[5] = b.y, e4[6] = b.z, e4[7] = b.w;
+      } else {
 #pragma unroll
-      for (int v = 0; v < 32; ++v) {
-        const int e = cb + v < M ? col_exp[cb + v] : 0;
-        if (e) r[v] = __float_as_uint(__uint_as_float(r[v]) * __int_as_float((e + 127) << 23));
+        for (int w = 0; w < 8; ++w) {
+          uint32_t x = 0;
+          for (int i = 0; i < 4; ++i)
+            if (cb + 4 * w + i < M) x |= (uint32_t)(uint8_t)col_exp[cb + 4 * w + i] << (8 * i);
+          e4[w] = x;
+        }
+      }
+      if ((e4[0] | e4[1] | e4[2] | e4[3] | e4[4] | e4[5] | e4[6] | e4[7]) != 0u) {
+#pragma unroll
+        for (int v = 0; v < 32; ++v) {
+          const int e = (int)(int8_t)(e4[v >> 2] >> (8 * (v & 3)));
+          if (e) r[v] = __float_as_uint(__uint_as_float(r[v]) * __int_as_float((e + 127) << 23));
+        }
       }
     }
     if (vec_ok && cb + 32 <= M) {
@@ -1142,50 +1152,73 @@ __global__ void __launch_bounds__(kWThreads, 1)
 template <int DT>
 __global__ void __launch_bounds__(256) widen_w_f16_kernel(const uint8_t* __restrict__ W, uint4* __restrict__ out,
                                                           long n16) {
-  for (long i = blockIdx.x * 256L + threadIdx.x; i < n16; i += (long)gridDim.x * 256L) {
-    const uint4 v = __ldcs(reinterpret_cast<const uint4*>(W) + i);   // 16 weights, read once
-    const uint2 lo = make_uint2(v.x, v.y), hi = make_uint2(v.z, v.w);
-    out[2 * i] = DT == kINT8 ? widen_i8x8(lo) : widen_e4m3x8(lo);
-    out[2 * i + 1] = DT == kINT8 ? widen_i8x8(hi) : widen_e4m3x8(hi);
+  // four 16-byte loads in flight per thread before any is converted
+  constexpr int U = 4;
+  const long stride = (long)gridDim.x * 256L;
+  for (long i0 = blockIdx.x * 256L + threadIdx.x; i0 < n16; i0 += U * stride) {
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long i = i0 + u * stride;
+      v[u] = i < n16 ? __ldcs(reinterpret_cast<const uint4*>(W) + i) : make_uint4(0, 0, 0, 0);   // read once
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const long i = i0 + u * stride;
+      if (i >= n16) break;
+      const uint2 lo = make_uint2(v[u].x, v[u].y), hi = make_uint2(v[u].z, v[u].w);
+      out[2 * i] = DT == kINT8 ? widen_i8x8(lo) : widen_e4m3x8(lo);
+      out[2 * i + 1] = DT == kINT8 ? widen_i8x8(hi) : widen_e4m3x8(hi);
+    }
   }
 }
 
-// mxfp4 weights [M,K] (E2M1, UE8M0 per 32) widened once to f16 [M,K], one warp
-// per weight row: the row's exponent offset c_m (the rule of mx_row_exp_kernel)
-// keeps E2M1 * 2^(s-127-c_m) exact in f16, and col_exp[m] = c_m tells the GEMM
-// epilogue to multiply output column m by 2^c_m.
-__global__ void __launch_bounds__(256) widen_mx_f16_kernel(const uint8_t* __restrict__ W,
-                                                           const uint8_t* __restrict__ wscale, int M, int K,
-                                                           uint4* __restrict__ out, int8_t* __restrict__ col_exp) {
-  const int m = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (m >= M) return;   // warp-uniform
-  const int kbpr = K / 32;
-  const uint8_t* srow = wscale + (size_t)m * kbpr;
-  int mn = 255, mx = 0;
-  for (int i = lane; i < kbpr; i += 32) {
-    const int sc = __ldg(srow + i);
-    mn = min(mn, sc);
-    mx = max(mx, sc);
-  }
+// mxfp4 weights [M,K] widened once to f16 in the [K,M] layout of the fp16
+// weights (the pair kernel then reads them MN-major, its fastest form).  A block
+// covers 128 rows x 64 K: each thread widens one 32-element block of one row
+// (row offsets c_m from mx_row_exp_kernel) into a shared [64 K][128] tile, which
+// goes out as 64 coalesced 256-byte rows of W16.
+constexpr int kWtM = 128, kWtK = 64;
+
+__global__ void __launch_bounds__(256) widen_mx_t_kernel(const uint8_t* __restrict__ W,
+                                                         const uint8_t* __restrict__ wscale,
+                                                         const int8_t* __restrict__ col_exp, int M, int K,
+                                                         __half* __restrict__ out) {
+  __shared__ __align__(16) __half tile[kWtK][kWtM];
+  const int t = threadIdx.x, r = t & 127, q = t >> 7;   // row of the tile, which 32 K
+  const int m0 = blockIdx.x * kWtM, k0 = blockIdx.y * kWtK;
+  const int m = m0 + r, kb = k0 / 32 + q, kbpr = K / 32;
+  uint32_t h[16];
+  if (m < M && kb < kbpr) {
+    const uint4 w = __ldcs(reinterpret_cast<const uint4*>(W + (size_t)m * (K / 2)) + kb);
+    const uint32_t mul = f16x2_pow2((int)__ldg(wscale + (size_t)m * kbpr + kb) - 127 - (int)col_exp[m]);
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = widen_e2m1x8(words[i], mul);
+      h[4 * i] = v.x;
+      h[4 * i + 1] = v.y;
+      h[4 * i + 2] = v.z;
+      h[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) h[i] = 0;
   }
-  int c = 0;
-  if (mx > 140) c = mx - 140;
-  else if (mn < 104) c = max(mn - 104, mx - 140);
-  if (lane == 0) col_exp[m] = (int8_t)c;
-  // one 16-byte block (32 E2M1, one scale) per lane and step -> 64 bytes of f16
-  const uint4* wrow = reinterpret_cast<const uint4*>(W + (size_t)m * (K / 2));
-  uint4* orow = out + (size_t)m * (K / 8);
-  for (int b = lane; b < kbpr; b += 32) {
-    const uint4 w = __ldcs(wrow + b);
-    const uint32_t mul = f16x2_pow2((int)__ldg(srow + b) - 127 - c);
-    orow[4 * b] = widen_e2m1x8(w.x, mul);
-    orow[4 * b + 1] = widen_e2m1x8(w.y, mul);
-    orow[4 * b + 2] = widen_e2m1x8(w.z, mul);
-    orow[4 * b + 3] = widen_e2m1x8(w.w, mul);
+  // element k = 32 q + 2 i (+1) of row r; a warp writes 32 consecutive rows per K
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    tile[32 * q + 2 * i][r] = __ushort_as_half((unsigned short)(h[i] & 0xFFFFu));
+    tile[32 * q + 2 * i + 1][r] = __ushort_as_half((unsigned short)(h[i] >> 16));
+  }
+  __syncthreads();
+  // 64 K rows x 16 chunks of 8 f16 (M % 8 == 0)
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int i = t + 256 * it, c = i & 15, kr = i >> 4;
+    const int k = k0 + kr, mc = m0 + 8 * c;
+    if (k < K && mc < M)
+      *reinterpret_cast<uint4*>(out + (size_t)k * M + mc) = *reinterpret_cast<const uint4*>(&tile[kr][8 * c]);
   }
 }
 
@@ -1459,7 +1492,7 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
     if (bn != 256) return false;
     if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
     if (dt == kINT8 || dt == kFP8) return K % 8 == 0 && M % 16 == 0;   // widened to f16 first
-    if (dt == kMXFP4) return K % 32 == 0;                               // widened to f16 [M,K] first
+    if (dt == kMXFP4) return K % 32 == 0 && M % 8 == 0;                 // widened to f16 [K,M] first
     if (dt == kI8I8 || dt == kF8F8) return K % 16 == 0 && M % 16 == 0;
     if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;   // kind::f8f6f4 on unpacked E2M1
     if (dt == kMX4X4) return K % 32 == 0;                  // block-scaled kinds
@@ -1587,6 +1620,7 @@ size_t tc_workspace(int dt, int bm, int bn, int N, int K, int M) {
 }
 
 int tc_launches(int dt, int bm) {
+  if (bm == 256 && dt == kMXFP4) return 3;   // row offsets, widen, GEMM
   if (dt == kMXFP4 || dt == kF4F4 || dt == kMX4X4 || dt == kMX8X4 || dt == kF8X4) return 2;
   if (bm == 256 && (dt == kINT8 || dt == kFP8)) return 2;
   return 1;
@@ -1611,13 +1645,17 @@ cudaError_t launch_widened_pair(const RunArgs& a) {
 cudaError_t launch_widened_mx_pair(const RunArgs& a) {
   const size_t wbytes = round256((size_t)a.K * a.M * 2);
   if (!a.ws || a.ws_bytes < wbytes + round256((size_t)a.M) || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
-  uint4* w16 = static_cast<uint4*>(a.ws);
+  __half* w16 = static_cast<__half*>(a.ws);
   int8_t* col_exp = static_cast<int8_t*>(a.ws) + wbytes;
-  widen_mx_f16_kernel<<<(a.M + 7) / 8, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), a.wscale, a.M, a.K,
-                                                           w16, col_exp);
+  mx_row_exp_kernel<<<(a.M + 7) / 8, 256, 0, a.stream>>>(a.wscale, a.M, a.K / 32, col_exp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_pair<kF16K, 256, 6>(a, w16, nullptr, nullptr, 0, 0, col_exp);
+  const dim3 grid((a.M + kWtM - 1) / kWtM, (a.K + kWtK - 1) / kWtK);
+  widen_mx_t_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), a.wscale, col_exp, a.M, a.K,
+                                                w16);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_pair<kFP16, 256, 6>(a, w16, nullptr, nullptr, 0, 0, col_exp);
 }
 
 }  // namespace
