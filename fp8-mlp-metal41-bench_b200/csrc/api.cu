@@ -442,6 +442,70 @@ int gemm_time_e2e(int device, int dtype, int tile, const void* hX, void* dX, con
   return rc;
 }
 
+int gemm_time_e2e_pipelined(int device, int dtype, int tile, const void* hX, void* dX0, void* dX1, const void* dW,
+                            void* dY0, void* dY1, void* hY, int N, int K, int M, const void* hxscale,
+                            void* dxscale0, void* dxscale1, const void* dwscale, void* workspace,
+                            size_t workspace_bytes, int warmup, int iters, float* total_ms) {
+  DevState* s = dev_state(device);
+  if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised", device);
+  if (!hX || !hY || !dX1 || !dY1 || iters < 1 || warmup < 0 || !total_ms)
+    return fail(GEMM_ERR_ARGS, "bad timing arguments");
+  int rc = validate(device, dtype, tile, dX0, dW, dY0, N, K, M, dxscale0, dwscale, workspace, workspace_bytes);
+  if (rc) return rc;
+  if (x_scaled(dtype) && (!hxscale || !dxscale1)) return fail(GEMM_ERR_ARGS, "%s needs X scale planes", kDtypeNames[dtype]);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  const size_t xb = dtype == kF4F4 || dtype == kMX4X4 ? (size_t)N * K / 2
+                    : (x_is_half(dtype) ? (size_t)N * K * 2 : (size_t)N * K);
+  const size_t xsb = x_scaled(dtype) ? (size_t)N * (K / 32) : 0;
+  const size_t yb = (size_t)N * M * 4;
+  void* dX[2] = {dX0, dX1};
+  void* dY[2] = {dY0, dY1};
+  void* dXS[2] = {dxscale0, dxscale1};
+  // copies in, GEMMs, copies out: three streams; events order each buffer set's reuse
+  cudaStream_t st = s->stream, sin = nullptr, sout = nullptr;
+  cudaEvent_t in_done[2] = {}, gemm_done[2] = {}, out_done[2] = {}, t0 = nullptr, t1 = nullptr;
+  bool ok = cudaStreamCreateWithFlags(&sin, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&sout, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreate(&t0) == cudaSuccess && cudaEventCreate(&t1) == cudaSuccess;
+  for (int b = 0; b < 2 && ok; ++b)
+    ok = cudaEventCreateWithFlags(&in_done[b], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&gemm_done[b], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&out_done[b], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) rc = cuda_fail(cudaGetLastError(), "pipeline streams / events");
+  for (int i = 0; i < warmup + iters && rc == GEMM_OK; ++i) {
+    const int b = i & 1;
+    if (i == warmup) cudaEventRecord(t0, sin);
+    cudaStreamWaitEvent(sin, gemm_done[b], 0);   // step i-2 has consumed this X set
+    cudaMemcpyAsync(dX[b], hX, xb, cudaMemcpyHostToDevice, sin);
+    if (xsb) cudaMemcpyAsync(dXS[b], hxscale, xsb, cudaMemcpyHostToDevice, sin);
+    cudaEventRecord(in_done[b], sin);
+    cudaStreamWaitEvent(st, in_done[b], 0);
+    cudaStreamWaitEvent(st, out_done[b], 0);     // step i-2 has copied this Y set out
+    rc = enqueue(s, dtype, tile, dX[b], dW, dY[b], N, K, M, dXS[b], dwscale, workspace, workspace_bytes, st);
+    cudaEventRecord(gemm_done[b], st);
+    cudaStreamWaitEvent(sout, gemm_done[b], 0);
+    cudaMemcpyAsync(hY, dY[b], yb, cudaMemcpyDeviceToHost, sout);
+    cudaEventRecord(out_done[b], sout);
+    if (i == warmup + iters - 1) cudaEventRecord(t1, sout);
+  }
+  if (sin && (e = cudaStreamSynchronize(sin)) != cudaSuccess && rc == GEMM_OK) rc = cuda_fail(e, "pipeline copies in");
+  if ((e = cudaStreamSynchronize(st)) != cudaSuccess && rc == GEMM_OK) rc = cuda_fail(e, "pipeline GEMMs");
+  if (sout && (e = cudaStreamSynchronize(sout)) != cudaSuccess && rc == GEMM_OK) rc = cuda_fail(e, "pipeline copies out");
+  if (rc == GEMM_OK) rc = check_dev_error(s, device);
+  if (rc == GEMM_OK && (e = cudaEventElapsedTime(total_ms, t0, t1)) != cudaSuccess) rc = cuda_fail(e, "event time");
+  for (int b = 0; b < 2; ++b) {
+    if (in_done[b]) cudaEventDestroy(in_done[b]);
+    if (gemm_done[b]) cudaEventDestroy(gemm_done[b]);
+    if (out_done[b]) cudaEventDestroy(out_done[b]);
+  }
+  if (t0) cudaEventDestroy(t0);
+  if (t1) cudaEventDestroy(t1);
+  if (sin) cudaStreamDestroy(sin);
+  if (sout) cudaStreamDestroy(sout);
+  return rc;
+}
+
 int gemm_peak_probe(int device, int kind, int reps, int iters, double* tflops_out) {
   DevState* s = dev_state(device);
   if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised", device);

@@ -22,7 +22,8 @@ EXPORTS = [
     "gemm_tile_index", "gemm_tile_supported", "gemm_default_tile", "gemm_check_layout",
     "gemm_workspace_size", "gemm_alloc", "gemm_free", "gemm_memset", "gemm_h2d", "gemm_d2h",
     "gemm_host_alloc", "gemm_host_free", "gemm_run", "gemm_sync", "gemm_time",
-    "gemm_time_e2e", "gemm_launches_per_run", "gemm_peak_probe", "gemm_run_noalloc",
+    "gemm_time_e2e", "gemm_time_e2e_pipelined", "gemm_launches_per_run", "gemm_peak_probe",
+    "gemm_run_noalloc",
     "gemm_quantize",
 ]
 
@@ -80,6 +81,9 @@ def _declare(L):
         "gemm_time_e2e": (c_int, [c_int, c_int, c_int, vp, vp, vp, vp, vp, c_int, c_int, c_int,
                                   vp, vp, vp, vp, c_size, c_int, c_int,
                                   ctypes.POINTER(ctypes.c_float)]),
+        "gemm_time_e2e_pipelined": (c_int, [c_int, c_int, c_int, vp, vp, vp, vp, vp, vp, vp, c_int, c_int,
+                                            c_int, vp, vp, vp, vp, vp, c_size, c_int, c_int,
+                                            ctypes.POINTER(ctypes.c_float)]),
         "gemm_launches_per_run": (c_int, [c_int, c_int, c_int, c_int, c_int]),
         "gemm_peak_probe": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
         "gemm_run_noalloc": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp,
@@ -269,6 +273,19 @@ def time_e2e(device, dtype, tile, hX, dX, dW, dY, hY, N, K, M, hxscale=None, dxs
                               as_ptr(dwscale), as_ptr(workspace), int(workspace_bytes), warmup,
                               iters, out), "gemm_time_e2e")
     return list(out)
+
+
+def time_e2e_pipelined(device, dtype, tile, hX, dX, dW, dY, hY, N, K, M, hxscale=None, dxscale=(None, None),
+                       dwscale=None, workspace=None, workspace_bytes=0, warmup=3, iters=10) -> float:
+    """Total ms of `iters` end-to-end steps overlapped two deep; dX, dY (and
+    dxscale) are pairs of device buffers used in turn."""
+    out = ctypes.c_float(0.0)
+    check(lib().gemm_time_e2e_pipelined(device, dtype, tile, as_ptr(hX), as_ptr(dX[0]), as_ptr(dX[1]),
+                                        as_ptr(dW), as_ptr(dY[0]), as_ptr(dY[1]), as_ptr(hY), N, K, M,
+                                        as_ptr(hxscale), as_ptr(dxscale[0]), as_ptr(dxscale[1]),
+                                        as_ptr(dwscale), as_ptr(workspace), int(workspace_bytes), warmup,
+                                        iters, ctypes.byref(out)), "gemm_time_e2e_pipelined")
+    return out.value
 
 
 def peak_probe(device: int, kind: int, reps: int = 4096, iters: int = 10) -> float:

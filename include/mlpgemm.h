@@ -162,6 +162,21 @@ int gemm_time_e2e(int device, int dtype, int tile, const void *hX, void *dX,
                   void *workspace, size_t workspace_bytes, int warmup, int iters,
                   float *ms_out);
 
+/* End-to-end throughput with consecutive steps overlapped.  Each step copies X
+ * (and xscale) from pinned host memory in on its own stream, runs the GEMM on
+ * the device's stream and copies Y out to pinned host memory on a third stream;
+ * two device sets of X / Y are used in turn, so that step i's Y copy overlaps
+ * step i+1's X copy and GEMM (the two copy directions run on separate engines).
+ * Every step still moves its own inputs in and its own result out.  After
+ * `warmup` untimed steps, *total_ms receives the time of `iters` steps, from the
+ * first timed copy in to the last copy out.  The serving-loop form of runOnce
+ * (main.swift:486-518) with the host copies that a plugin host adds. */
+int gemm_time_e2e_pipelined(int device, int dtype, int tile, const void *hX, void *dX0, void *dX1,
+                            const void *dW, void *dY0, void *dY1, void *hY, int N, int K, int M,
+                            const void *hxscale, void *dxscale0, void *dxscale1, const void *dwscale,
+                            void *workspace, size_t workspace_bytes, int warmup, int iters,
+                            float *total_ms);
+
 /* Per-launch kernel time of the dominant kernel inside gemm_time's loop, and
  * the number of kernels one gemm_run launches (for the roofline report). */
 int gemm_launches_per_run(int dtype, int tile, int N, int K, int M);

@@ -244,3 +244,50 @@ def test_pair_tiles_deterministic(gemm, dtype):
     b, _, _ = run_case(gemm, dtype, "256x256", N, K, M, ops=ops)
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     assert_close(dtype, a, ref)
+
+
+@pytest.mark.parametrize("dtype", ["i8i8", "mxfp4/a8"])
+def test_e2e_timing_moves_the_result(gemm, dtype):
+    # both end-to-end timers copy X in and Y out on every step; the host Y they
+    # leave behind is the GEMM's result, and the overlapped loop is not slower
+    # per step than the serial one
+    import ctypes
+    G = gemm
+    N, K, M = 512, 1024, 768
+    ops = Operands(N, K, M, "seeded", 5)
+    dt, ti = F.CODE[dtype], G.tile_index("128x256")
+    xh, xs, ws = ops.X(dtype), ops.xscale(dtype), ops.wscale(dtype)
+    dX = [G.DeviceBuffer(0, xh.nbytes) for _ in range(2)]
+    dY = [G.DeviceBuffer(0, N * M * 4).zero() for _ in range(2)]
+    dXS = [G.DeviceBuffer(0, xs.nbytes) for _ in range(2)] if xs is not None else [None, None]
+    W = G.DeviceBuffer(0, ops.W(dtype).nbytes).upload(ops.W(dtype))
+    WS = G.DeviceBuffer(0, ws.nbytes).upload(ws) if ws is not None else None
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+    L = G.lib()
+    hX, hY = L.gemm_host_alloc(xh.nbytes), L.gemm_host_alloc(N * M * 4)
+    hXS = L.gemm_host_alloc(xs.nbytes) if xs is not None else None
+    try:
+        ctypes.memmove(hX, xh.ctypes.data, xh.nbytes)
+        if xs is not None:
+            ctypes.memmove(hXS, xs.ctypes.data, xs.nbytes)
+        ref = oracle.full_reference(dtype, xh, ops.W(dtype), xs, ws, N, K, M)
+        out_t = np.int32 if dtype == "i8i8" else np.float32
+        for run in ("serial", "pipelined"):
+            ctypes.memset(hY, 0, N * M * 4)
+            if run == "serial":
+                ms = G.time_e2e(0, dt, ti, hX, dX[0], W, dY[0], hY, N, K, M, hXS, dXS[0], WS, WSP, wsb,
+                                warmup=1, iters=4)
+                per_step = sum(ms) / len(ms)
+            else:
+                total = G.time_e2e_pipelined(0, dt, ti, hX, dX, W, dY, hY, N, K, M, hXS, dXS, WS, WSP, wsb,
+                                             warmup=1, iters=8)
+                assert total > 0
+                assert total / 8 <= 1.5 * per_step
+            out = np.ctypeslib.as_array(ctypes.cast(hY, ctypes.POINTER(ctypes.c_uint32)), (N * M,))
+            assert_close(dtype, out.view(out_t).reshape(N, M).copy(), ref)
+    finally:
+        L.gemm_host_free(hX)
+        L.gemm_host_free(hY)
+        if hXS:
+            L.gemm_host_free(hXS)
