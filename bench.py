@@ -315,13 +315,24 @@ def ours(a):
     flops = 2.0 * N * K * M
     value = DU.weak_scaling_rate(flops, world, a.steps, total_ms)
 
-    # end to end through the C ABI: pinned host X in, device GEMM, host Y out
-    e2e = None
-    if rank == 0:
-        e2e = e2e_measure(G, local, dtype, dt, ti, ops, X, W, XS, WS, Y, WSP, wsb, N, K, M, a)
+    # end to end through the C ABI: pinned host X in, device GEMM, host Y out,
+    # every rank at once (they share the host's memory); the job's rate is set
+    # by the slowest rank, as for `value`
     if dist is not None:
         dist.barrier()
+    e2e = e2e_measure(G, local, dtype, dt, ti, ops, X, W, XS, WS, Y, WSP, wsb, N, K, M, a)
+    if dist is not None:
+        t_max = DU.reduce_max(dist, e2e["ms_per_step"], "cuda")
+        t_ser = DU.reduce_max(dist, e2e["serial"]["ms_per_step"], "cuda")
+        dist.barrier()
         dist.destroy_process_group()
+    else:
+        t_max, t_ser = e2e["ms_per_step"], e2e["serial"]["ms_per_step"]
+    flops_job = 2.0 * N * K * M * world
+    e2e.update({"value": flops_job / (t_max / 1e3) / 1e12, "ms_per_step": t_max,
+                "h2d_bytes_per_step": e2e["h2d_bytes_per_step"] * world,
+                "d2h_bytes_per_step": e2e["d2h_bytes_per_step"] * world, "ranks": world})
+    e2e["serial"].update({"value": flops_job / (t_ser / 1e3) / 1e12, "ms_per_step": t_ser})
     if rank != 0:
         return 0 if ok else 3
 
