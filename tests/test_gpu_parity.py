@@ -300,3 +300,29 @@ def test_f4f4_pair_ragged_m(gemm, M):
     N, K = 384, 1024
     out, ref, _ = run_case(gemm, "f4f4", "256x256", N, K, M)
     assert_close("f4f4", out, ref)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "i8i8", "f8f8"])
+@pytest.mark.parametrize("shape", [(256, 256, 19200), (512, 256, 14080)])
+def test_pair_tiles_many_waves(gemm, dtype, shape):
+    # more 256x256 tiles than CTA pairs (75 and 110 tiles: the persistent grid
+    # takes several waves, the last one short); two calls give the same bits
+    G = gemm
+    N, K, M = shape
+    ops = Operands(N, K, M, "seeded", 8)
+    dt, ti = F.CODE[dtype], G.tile_index("256x256")
+    X = G.DeviceBuffer(0, ops.X(dtype).nbytes).upload(ops.X(dtype))
+    W = G.DeviceBuffer(0, ops.W(dtype).nbytes).upload(ops.W(dtype))
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+    outs = []
+    for _ in range(2):
+        Y = G.DeviceBuffer(0, N * M * 4).zero()
+        G.run(0, dt, ti, X, W, Y, N, K, M, None, None, WSP, wsb)
+        G.sync(0)
+        o = np.empty((N, M), dtype=np.int32 if dtype == "i8i8" else np.float32)
+        Y.download(o)
+        outs.append(o)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), None, None, N, K, M)
+    assert_close(dtype, outs[1], ref)
