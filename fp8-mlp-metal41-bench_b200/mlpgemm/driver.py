@@ -8,8 +8,9 @@ header lines, autotune lines, profile file and table (main.swift:616-669),
 same exit codes (1 bad arguments / GPU error, 2 library load failure,
 3 result mismatch).
 
-Added flags (all optional): --gpus 1|2|4|8 (M-sharded across GPUs; run
-under torchrun), --allgather (gather Y over NCCL, timed separately),
+Added flags (all optional): --gpus 1|2|4|8 (sharded across GPUs; run
+under torchrun), --shard m|n (split W's columns, the default, or X's rows),
+--allgather (gather Y over NCCL, timed separately),
 --data ref|seeded, --seed S, --rotate R (R weight copies used round-robin),
 --flush (overwrite a >L2 buffer before every timed iteration).
 """
@@ -58,6 +59,7 @@ class Args:
     autotune: bool = False
     use_profile: bool = True
     gpus: int = 1
+    shard: str = "m"        # "m": columns of W per GPU; "n": rows of X per GPU
     allgather: bool = False
     data: str = "seeded"
     seed: int = 0
@@ -119,6 +121,12 @@ def parse_args(argv, tiles=None) -> Args:
                 a.dtypes = [name]
             else:
                 raise BenchExit(1, f"Unknown --dtype {name} ({', '.join(F.DTYPES)}, all)")
+            continue
+        if key == "--shard":
+            a.shard = argv[i].lower()
+            i += 1
+            if a.shard not in ("m", "n"):
+                raise BenchExit(1, f"Unknown --shard {a.shard} (m, n)")
             continue
         if key == "--data":
             a.data = argv[i]

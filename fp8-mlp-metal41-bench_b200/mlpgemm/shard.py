@@ -1,4 +1,4 @@
-"""M-sharded GEMM across the GPUs of one node (strong scaling).
+"""M- or N-sharded GEMM across the GPUs of one node (strong scaling).
 
 Run under torchrun, one process per GPU:
 
@@ -25,6 +25,12 @@ no exchange inside it:
     Y on one CUDA stream, and each finished chunk is all-gathered by NCCL on
     a second stream while the next chunk computes.  The pipeline's own
     end-to-end time is reported beside gemm + all-gather run back to back.
+
+`--shard n` splits the rows of X instead (run_shape_rows): W is replicated
+(generated on rank 0, broadcast once), X rows are dealt out block-cyclically
+(row_blocks), and every rank's block of Y already sits at its final rows, so
+the all-gather is in place into Y[N,M] with no permute, and each round of
+the pipeline gathers straight into Y as well.
 
 torch.distributed is plumbing here (device buffers, NCCL, barriers); the
 GEMM itself is libgemm.so through its C ABI.
@@ -71,6 +77,41 @@ def shard_plan(M: int, world: int):
         m0 = min(g * base, M)
         out.append((m0, min(m0 + base, M) - m0))
     return out
+
+
+def row_blocks(N: int, world: int, chunks: int = 1):
+    """Block-cyclic row plan of the N-sharded GEMM: (ch, rounds, blocks).
+
+    Rows of X and Y go out in rounds of `world` blocks of `ch` rows each. In
+    round c, rank g owns rows [c*world*ch + g*ch, +ch). A round's blocks are
+    therefore consecutive rows of the row-major Y[N,M], and an in-place
+    all-gather of the round puts every rank's block at its final rows: the
+    gathered buffer is Y itself, with no permute. blocks[g] lists
+    (row0, rows) per round; rows are clamped at N, and a block past the end
+    has 0 rows. `ch` is rounded up to a multiple of 128 (one tensor-core
+    tile row) above 128 rows. `chunks` is lowered until no block is under
+    128 rows, except when N itself gives each rank fewer than 128."""
+    world = max(1, world)
+    chunks = max(1, min(chunks, N // (world * 128)))
+    ch = max(1, -(-N // (world * chunks)))
+    if ch > 128:
+        ch = -(-ch // 128) * 128
+    rounds = max(1, -(-N // (world * ch)))
+    blocks = []
+    for g in range(world):
+        mine = []
+        for c in range(rounds):
+            r0 = c * world * ch + g * ch
+            mine.append((min(r0, N), max(0, min(ch, N - r0))))
+        blocks.append(mine)
+    return ch, rounds, blocks
+
+
+def gather_round(dist, Y2d, c: int, world: int, rank: int, ch: int):
+    """In-place all-gather of round c of a block-cyclic Y (rows padded to
+    rounds*world*ch): this rank's block is already at its rows."""
+    rnd = Y2d[c * world * ch:(c + 1) * world * ch]
+    dist.all_gather_into_tensor(rnd, rnd[rank * ch:(rank + 1) * ch])
 
 
 def row_chunks(N: int, chunks: int):
@@ -198,7 +239,7 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
             vs = "-"
         rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
                         rel, gpus=world, allgather_ms=ag_ms))
-        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, width, med_max * 1000.0,
+        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, f"{width}c", med_max * 1000.0,
                       extra_pipe.get(dtype)))
     return rows, extra
 
@@ -249,6 +290,178 @@ def _pipeline(a, torch, dist, world, local, dt, ti, tile, X, XS, Wt, WS, WSP, ws
     return float(t.item())
 
 
+class _RowsAt:
+    """Y[n, m] lookups on chosen global rows of a device Y (for check_samples)."""
+
+    def __init__(self, Y2d, rows, row0: int = 0):
+        self.rows = {n: Y2d[n - row0].cpu().numpy() for n in rows}
+
+    def __getitem__(self, nm):
+        n, m = nm
+        return self.rows[n][m]
+
+
+def _bcast_timed(torch, dist, buf):
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dist.broadcast(buf, src=0)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def _rank_rows(arr, row_bytes: int, blocks, ch: int):
+    """This rank's rows of a row-major byte array, one ch-row slot per round
+    (zero past N)."""
+    flat = arr.view(np.uint8).reshape(-1)
+    out = np.zeros(len(blocks) * ch * row_bytes, dtype=np.uint8)
+    for c, (r0, h) in enumerate(blocks):
+        if h:
+            out[c * ch * row_bytes:(c * ch + h) * row_bytes] = flat[r0 * row_bytes:(r0 + h) * row_bytes]
+    return out
+
+
+def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
+    """The N-sharded GEMM: rows of X split block-cyclically (row_blocks), W
+    replicated. Each rank derives its X rows from the seeded generator; W is
+    generated on rank 0 and broadcast once over NCCL (`bcast_ms`). The
+    --allgather collective writes straight into Y[N,M] (gather_round), with
+    no permute; the pipeline overlaps each round's all-gather with the next
+    round's GEMM."""
+    N, K, M = shape.N, shape.K, shape.M
+    flops = 2.0 * N * K * M
+    dev = torch.device("cuda", local)
+    rows, extra, medians = [], [], {}
+    for dtype in a.dtypes:
+        if not F.layout_ok(dtype, N, K, M):
+            raise BenchExit(1, f"{dtype} needs even X/W counts and K a multiple of 32 "
+                               f"(128 for FP8 × MXFP4)")
+        if dtype in F.X_FP4 and K % 2:
+            raise BenchExit(1, f"row sharding of packed 4-bit {dtype} X needs an even K")
+        ops = Operands(N, K, M, a.data, a.seed)
+        dt = F.CODE[dtype]
+        ch, rounds, blocks = row_blocks(N, world, 1)
+        r0, h = blocks[rank][0]
+        xrow = F.x_bytes(dtype, 1, K)
+        srow = K // 32 if dtype in F.X_SCALED else 0
+        tile = choose_tile(a, profile, dtype, max(h, 1), K, M)
+        ti = G.tile_index(tile)
+        # W: generated on rank 0 and broadcast (timed); X rows: this rank's own
+        Wh = ops.W(dtype).view(np.uint8).reshape(-1)
+        Wt = torch.empty(Wh.size, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            Wt.copy_(torch.from_numpy(Wh.copy()))
+        bcast_ms = _bcast_timed(torch, dist, Wt)
+        ws = ops.wscale(dtype)
+        WS = None
+        if ws is not None:
+            WS = torch.from_numpy(ws.copy()).to(dev)
+            dist.broadcast(WS, src=0)
+        Xr = torch.from_numpy(_rank_rows(ops.X(dtype), xrow, blocks[rank], ch)).to(dev)
+        XS = None
+        if srow:
+            XS = torch.from_numpy(_rank_rows(ops.xscale(dtype), srow, blocks[rank], ch)).to(dev)
+        ydt = torch.int32 if dtype == "i8i8" else torch.float32
+        Y = torch.zeros(rounds * world * ch, M, dtype=ydt, device=dev)
+        slot = Y[rank * ch:rank * ch + ch]
+        wsb = G.workspace_size(dt, ti, h, K, M) if h > 0 else 0
+        WSP = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev) if wsb else None
+        torch.cuda.synchronize()
+        med = 0.0
+        if h > 0:
+            ms = G.time(local, dt, ti, Xr, [Wt], slot, h, K, M, xscale=XS, wscales=[WS] if WS is not None else None,
+                        workspace=WSP, workspace_bytes=wsb, warmup=a.warmup, iters=shape.iters)
+            med = sorted(ms)[len(ms) // 2]
+        t = torch.tensor([med], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        med_max = float(t.item()) / 1000.0
+        medians[dtype] = med_max
+        bm, bn = tile_dims(tile)
+        rel = 0.0
+        if h > 0:   # sample points of this rank's own rows
+            pts = [(r0 + n, m) for n, m in sample_points(h, M, bm, bn)]
+            rel = check_samples(ops, dtype, _RowsAt(slot, {n for n, _ in pts}, r0), pts, shape.name)
+        r = torch.tensor([rel], dtype=torch.float64, device=dev)
+        dist.all_reduce(r, op=dist.ReduceOp.MAX)
+        rel = float(r.item())
+        ag_ms = pipe_ms = None
+        if a.allgather:
+            times = []
+            for _ in range(6):   # one warm-up, then the median of 5
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gather_round(dist, Y, 0, world, rank, ch)
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            t = torch.tensor([sorted(times[1:])[2]], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ag_ms = float(t.item())
+            # every rank now holds Y[N,M] in place: check sample points of all of it
+            pts = sample_points(N, M, bm, bn) + [(b[0][0], M - 1) for b in blocks if b[0][1]]
+            check_samples(ops, dtype, _RowsAt(Y, {n for n, _ in pts}), pts, shape.name)
+            pipe_ms = _pipeline_rows(a, torch, dist, world, rank, local, ops, dtype, dt, tile, Wt, WS, Y[:N])
+        vs = "1.000" if dtype == "fp16" else ("%.3f" % (medians["fp16"] / med_max) if "fp16" in medians else "-")
+        rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
+                        rel, gpus=world, allgather_ms=ag_ms))
+        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, f"{ch}r", med_max * 1000.0, pipe_ms))
+    return rows, extra
+
+
+def _pipeline_rows(a, torch, dist, world, rank, local, ops, dtype, dt, tile, Wt, WS, Yref, chunks=4, reps=5):
+    """N-sharded GEMM over `chunks` block-cyclic rounds on one stream, each
+    round all-gathered in place into Y on a second stream as soon as this
+    rank's block of it is done; returns the median over `reps` of the max
+    over ranks of the end-to-end event time (ms), after checking that the
+    gathered Y matches the one-round result `Yref`."""
+    N, K, M = Yref.shape[0], ops.K, ops.M
+    dev = torch.device("cuda", local)
+    ch, rounds, blocks = row_blocks(N, world, chunks)
+    xrow = F.x_bytes(dtype, 1, K)
+    srow = K // 32 if dtype in F.X_SCALED else 0
+    Xr = torch.from_numpy(_rank_rows(ops.X(dtype), xrow, blocks[rank], ch)).to(dev)
+    XS = torch.from_numpy(_rank_rows(ops.xscale(dtype), srow, blocks[rank], ch)).to(dev) if srow else None
+    Y = torch.zeros(rounds * world * ch, M, dtype=Yref.dtype, device=dev)
+    ti = G.tile_index(tile)
+    if not G.tile_supported(dt, ti, ch, K, M):
+        ti = G.tile_index(choose_tile(a, {}, dtype, ch, K, M))
+    wsb = G.workspace_size(dt, ti, ch, K, M)
+    WSP = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev) if wsb else None
+    gemm_s, comm_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    cur = torch.cuda.current_stream(dev)
+    times = []
+    for _ in range(reps + 1):
+        gemm_s.wait_stream(cur)
+        comm_s.wait_stream(cur)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(gemm_s)
+        comm_s.wait_event(e0)
+        for c, (r0, h) in enumerate(blocks[rank]):
+            if h:
+                G.run(local, dt, ti, Xr.data_ptr() + c * ch * xrow,
+                      Wt, Y[c * world * ch + rank * ch].data_ptr(), h, K, M,
+                      None if XS is None else XS.data_ptr() + c * ch * srow, WS, WSP, wsb,
+                      stream=gemm_s.cuda_stream)
+            done = torch.cuda.Event()
+            done.record(gemm_s)
+            comm_s.wait_event(done)
+            with torch.cuda.stream(comm_s):
+                gather_round(dist, Y, c, world, rank, ch)
+        e1.record(comm_s)
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1))
+    if Yref.dtype == torch.int32:
+        assert torch.equal(Y[:N], Yref)
+    else:
+        assert torch.allclose(Y[:N], Yref, rtol=1e-4, atol=1e-4)
+    med = sorted(times[1:])[len(times[1:]) // 2]
+    t = torch.tensor([med], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 class _SubOps:
     """Operands view of one column block (for the sample-point check)."""
 
@@ -278,7 +491,8 @@ def main_sharded(a, shapes) -> int:
         print(f"loaded: {G.LIB_PATH}")
         print(f"architecture: {arch}")
         print(f"tiles: {'--tile ' + a.tile if a.tile else 'built-in defaults per shard'}")
-        print(f"data: {a.data} seed={a.seed}  sharding: M across {world} GPUs"
+        axis = "N (rows of X, block-cyclic; W replicated)" if a.shard == "n" else "M (columns of W)"
+        print(f"data: {a.data} seed={a.seed}  sharding: {axis} across {world} GPUs"
               + (", Y all-gathered over NCCL" if a.allgather else ""))
         sys.stdout.flush()
     rows, extra = [], []
@@ -289,7 +503,8 @@ def main_sharded(a, shapes) -> int:
     torch.cuda.synchronize()
     try:
         for s in shapes:
-            r, e = run_shape(a, s, torch, dist, world, rank, local, {})
+            run = run_shape_rows if a.shard == "n" else run_shape
+            r, e = run(a, s, torch, dist, world, rank, local, {})
             rows += r
             extra += e
     finally:
@@ -300,14 +515,14 @@ def main_sharded(a, shapes) -> int:
         for line in render_table(rows):
             print(line)
         print("")
-        hdr = " ".join([_c("shape", 8), _c("dtype", 9), _c("gpus", 4, True), _c("cols/gpu", 8, True),
+        hdr = " ".join([_c("shape", 8), _c("dtype", 9), _c("gpus", 4, True), _c("block/gpu", 9, True),
                         _c("bcast_ms", 10, True), _c("allgather_ms", 12, True),
                         _c("gemm+ag_ms", 11, True), _c("pipeline_ms", 11, True)])
         print(hdr)
         print("-" * len(hdr))
         for (sh, d, g, b, ag, w, gm, pp) in extra:
             seq = "-" if ag is None else "%.4f" % (gm + ag)
-            print(" ".join([_c(sh, 8), _c(d, 9), _c(str(g), 4, True), _c(str(w), 8, True),
+            print(" ".join([_c(sh, 8), _c(d, 9), _c(str(g), 4, True), _c(w, 9, True),
                             _c("%.4f" % b, 10, True), _c("-" if ag is None else "%.4f" % ag, 12, True),
                             _c(seq, 11, True), _c("-" if pp is None else "%.4f" % pp, 11, True)]))
         print("ok")
@@ -320,4 +535,4 @@ def _c(t, w, right=False):
     return p + t if right else t + p
 
 
-__all__ = ["main_sharded", "shard_plan", "row_chunks", "table_line"]
+__all__ = ["main_sharded", "shard_plan", "row_chunks", "row_blocks", "gather_round", "table_line"]

@@ -79,3 +79,61 @@ def test_pipeline_row_chunks():
 
 def test_strong_scaling_rate():
     assert DU.strong_scaling_rate(2.0, 1.0) == pytest.approx(2e-9)
+
+
+def test_row_blocks_cover_rows():
+    from mlpgemm.shard import row_blocks
+    for N in (1, 7, 16, 100, 128, 300, 1000, 2048, 4096):
+        for G in (1, 2, 4, 8):
+            for c in (1, 2, 4):
+                ch, rounds, blocks = row_blocks(N, G, c)
+                assert len(blocks) == G and all(len(b) == rounds for b in blocks)
+                seen = []
+                for g in range(G):
+                    for k, (r0, h) in enumerate(blocks[g]):
+                        assert 0 <= h <= ch
+                        if h:   # a block sits at its own rows of the round
+                            assert r0 == k * G * ch + g * ch
+                            seen += range(r0, r0 + h)
+                assert sorted(seen) == list(range(N))
+                if ch > 128:
+                    assert ch % 128 == 0
+                if rounds > 1:
+                    assert ch >= 128
+    assert row_blocks(2048, 8, 1)[:2] == (256, 1)
+    assert row_blocks(2048, 2, 4)[:2] == (256, 4)
+    assert row_blocks(2048, 8, 4)[:2] == (128, 2)
+
+
+def _rows_worker(rank, world, port, out):
+    """Each rank computes its block-cyclic rows of Y = X @ W and gathers the
+    rounds in place; the result must be X @ W with no permute."""
+    from mlpgemm.shard import gather_round, row_blocks
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        res = {}
+        for N, chunks in ((300, 1), (1024, 4), (5, 1), (1000, 2)):
+            g = torch.Generator().manual_seed(N)
+            X = torch.randint(-8, 8, (N, 24), generator=g, dtype=torch.int64)
+            W = torch.randint(-8, 8, (24, 40), generator=g, dtype=torch.int64)
+            ch, rounds, blocks = row_blocks(N, world, chunks)
+            Y = torch.zeros(rounds * world * ch, 40, dtype=torch.int64)
+            for c, (r0, h) in enumerate(blocks[rank]):
+                if h:
+                    Y[c * world * ch + rank * ch:c * world * ch + rank * ch + h] = X[r0:r0 + h] @ W
+                gather_round(dist, Y, c, world, rank, ch)
+            res[(N, chunks)] = bool(torch.equal(Y[:N], X @ W))
+        out[rank] = res
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_row_shard_gather_in_place():
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_rows_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    for r in range(world):
+        assert all(out[r].values()), out[r]

@@ -93,6 +93,12 @@ def test_parse_args_quirks():
     assert e.value.code == 1 and "Unknown --tile 64x32" in e.value.msg
     a = D.parse_args(["--peak", "--iters", "3"], tiles)     # peak probe mode (tune/peak.swift)
     assert a.peak and a.iters == 3 and not a.suite
+    a = D.parse_args(["--gpus", "2", "--shard", "N", "--allgather"], tiles)
+    assert a.gpus == 2 and a.shard == "n" and a.allgather
+    assert D.parse_args([], tiles).shard == "m"
+    with pytest.raises(D.BenchExit) as e:
+        D.parse_args(["--shard", "k"], tiles)
+    assert e.value.code == 1
 
 
 def test_sample_points_match_oracle():
