@@ -131,8 +131,10 @@ int check_dev_error(DevState* s, int device) {
 
 int enqueue(DevState* s, int dt, int tile, const void* X, const void* W, void* Y, int N, int K,
             int M, const void* xscale, const void* wscale, void* ws, size_t ws_bytes,
-            cudaStream_t st) {
+            cudaStream_t st, void* const* ypeers = nullptr, int npeers = 0) {
   RunArgs a;
+  a.ypeers = ypeers;
+  a.npeers = npeers;
   a.dt = dt;
   a.X = X;
   a.W = W;
@@ -349,6 +351,65 @@ int gemm_run(int device, int dtype, int tile, const void* X, const void* W, void
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   return enqueue(s, dtype, tile, X, W, Y, N, K, M, xscale, wscale, workspace, workspace_bytes,
                  static_cast<cudaStream_t>(stream));
+}
+
+int gemm_run_gather(int device, int dtype, int tile, const void* X, const void* W, void* Y, int N, int K,
+                    int M, const void* xscale, const void* wscale, void* workspace, size_t workspace_bytes,
+                    void* const* ypeers, int npeers, void* stream) {
+  DevState* s = dev_state(device);
+  if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised (call gemm_init)", device);
+  int rc = validate(device, dtype, tile, X, W, Y, N, K, M, xscale, wscale, workspace, workspace_bytes);
+  if (rc) return rc;
+  if (npeers < 0 || npeers > GEMM_MAX_PEERS) return fail(GEMM_ERR_ARGS, "npeers %d not in 0..%d", npeers, GEMM_MAX_PEERS);
+  if (npeers && !ypeers) return fail(GEMM_ERR_ARGS, "null peer list");
+  for (int i = 0; i < npeers; ++i)
+    if (!ypeers[i] || (reinterpret_cast<uintptr_t>(ypeers[i]) & 15u))
+      return fail(GEMM_ERR_ARGS, "peer Y %d is null or not 16-byte aligned", i);
+  if (npeers && (kTiles[tile].kind != kTileTC || !tc_gather_supported(dtype, kTiles[tile].bm)))
+    return fail(GEMM_ERR_ARGS, "tile %s has no fused all-gather for %s", kTiles[tile].name, kDtypeNames[dtype]);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return enqueue(s, dtype, tile, X, W, Y, N, K, M, xscale, wscale, workspace, workspace_bytes,
+                 static_cast<cudaStream_t>(stream), ypeers, npeers);
+}
+
+int gemm_gather_supported(int dtype, int tile) {
+  return valid_dtype(dtype) && valid_tile(tile) && kTiles[tile].kind == kTileTC &&
+         tc_gather_supported(dtype, kTiles[tile].bm);
+}
+
+int gemm_peer_alloc(int device, size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle) return fail(GEMM_ERR_ARGS, "null output");
+  *ptr = nullptr;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaMalloc(ptr, bytes ? bytes : 1);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (peer buffer)");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(h) == GEMM_PEER_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return GEMM_OK;
+}
+
+int gemm_peer_open(int device, const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(GEMM_ERR_ARGS, "null argument");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? GEMM_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int gemm_peer_close(int device, void* ptr) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? GEMM_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
 }
 
 int gemm_sync(int device, void* stream) {

@@ -126,7 +126,15 @@ struct TcParams {
   int N, K, M;
   int tiles_m, tiles_n, num_kb;
   int* dev_err;
+  uint32_t* peer[kMaxPeers];   // peer Y bases: every Y store is repeated at the same offset
+  int npeers;
 };
+
+void set_peers(TcParams& p, const RunArgs& a) {
+  p.npeers = a.npeers;
+  for (int i = 0; i < kMaxPeers; ++i)
+    p.peer[i] = i < a.npeers ? static_cast<uint32_t*>(a.ypeers[i]) : nullptr;
+}
 
 constexpr uint32_t pow2_cols(int c) {
   return c <= 32 ? 32u : c <= 64 ? 64u : c <= 128 ? 128u : c <= 256 ? 256u : 512u;
@@ -253,9 +261,26 @@ __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb
 // is stored, and `release` runs as soon as the last load has completed, so the
 // next tile's MMAs may overwrite the accumulator while the last chunk is still
 // being stored.
+//
+// With peers (the fused all-gather), each chunk is stored again at the same
+// offset (`yoff`, the row's start) in every peer's Y over NVLink; the stores
+// are plain posted writes, made visible to the peers by the kernel's end.
+__device__ __forceinline__ void store_chunk(uint32_t* yrow, const uint32_t (&r)[32], int cb, int M, bool vec_ok) {
+  if (vec_ok && cb + 32 <= M) {
+    uint4* dst = reinterpret_cast<uint4*>(yrow + cb);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+  } else {
+#pragma unroll
+    for (int v = 0; v < 32; ++v)
+      if (cb + v < M) yrow[cb + v] = r[v];
+  }
+}
+
 template <int NCH, typename Release>
 __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, int col0, int M, bool row_ok,
-                                               const int8_t* col_exp, Release release) {
+                                               const int8_t* col_exp, const TcParams& p, size_t yoff,
+                                               Release release) {
   const bool vec_ok = (M % 4) == 0;
   auto store = [&](uint32_t (&r)[32], int c) {
     const int cb = col0 + c * 32;
@@ -285,14 +310,11 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
         }
       }
     }
-    if (vec_ok && cb + 32 <= M) {
-      uint4* dst = reinterpret_cast<uint4*>(yrow + cb);
+    store_chunk(yrow, r, cb, M, vec_ok);
+    if (p.npeers) {
 #pragma unroll
-      for (int v = 0; v < 8; ++v) dst[v] = make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-    } else {
-#pragma unroll
-      for (int v = 0; v < 32; ++v)
-        if (cb + v < M) yrow[cb + v] = r[v];
+      for (int i = 0; i < kMaxPeers; ++i)
+        if (i < p.npeers) store_chunk(p.peer[i] + yoff, r, cb, M, vec_ok);
     }
   };
   static_assert(NCH % 2 == 0, "chunks come in pairs");
@@ -497,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_COLS), yrow, col0,
-                              p.M, row_ok, p.col_exp, [&] {
+                              p.M, row_ok, p.col_exp, p, (size_t)row * p.M, [&] {
                                 tc_fence_before();
                                 mbar_arrive(&bars->acc_empty[buf]);
                               });
@@ -812,7 +834,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN), yrow, col0, p.M,
-                              row_ok, p.col_exp, [&] {
+                              row_ok, p.col_exp, p, (size_t)row * p.M, [&] {
                                 tc_fence_before();
                                 __syncwarp();
                                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
@@ -1338,6 +1360,7 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   p.tiles_n = (a.M + BN - 1) / BN;
   p.num_kb = (a.K + C::K_PER_STAGE - 1) / C::K_PER_STAGE;
   p.dev_err = a.dev_err;
+  set_peers(p, a);
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_gemm_kernel<DT, BN, STAGES>;
@@ -1403,6 +1426,7 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   p.tiles_n = (a.M + BN - 1) / BN;
   p.num_kb = (a.K + C::K_PER_STAGE - 1) / C::K_PER_STAGE;
   p.dev_err = a.dev_err;
+  set_peers(p, a);
   const int tiles = p.tiles_m * p.tiles_n;
   auto k = tc_gemm_pair_kernel<DT, BN, STAGES>;
   static unsigned attr_mask = 0;
@@ -1660,8 +1684,16 @@ cudaError_t launch_widened_mx_pair(const RunArgs& a) {
 
 }  // namespace
 
+bool tc_gather_supported(int dt, int bm) {
+  return bm == 256 || !(dt == kINT8 || dt == kFP8 || dt == kMXFP4);
+}
+
 cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
   if (!tc_supported(a.dt, bm, bn, a.N, a.K, a.M)) return cudaErrorInvalidValue;
+  if (a.npeers < 0 || a.npeers > kMaxPeers || (a.npeers && !tc_gather_supported(a.dt, bm)))
+    return cudaErrorInvalidValue;
+  for (int i = 0; i < a.npeers; ++i)
+    if (!a.ypeers || !aligned(a.ypeers[i], 16)) return cudaErrorInvalidValue;
   if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
   if (bm == 256) {
     switch (a.dt) {

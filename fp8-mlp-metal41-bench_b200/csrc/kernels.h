@@ -20,7 +20,14 @@ struct RunArgs {
   cudaStream_t stream;
   int* dev_err;      // device error word (bounded-wait timeouts)
   int num_sms;
+  // Fused all-gather: the tensor-core epilogue also stores every Y element at
+  // the same offset from each of these peer base pointers (other GPUs' Y
+  // buffers mapped into this context; see gemm_run_gather).
+  void* const* ypeers = nullptr;
+  int npeers = 0;
 };
+
+constexpr int kMaxPeers = 7;   // peers of one rank in an 8-GPU node
 
 // ---- CUDA-core split-K GEMV (thin rows; also the any-shape fallback) --------
 // Up to 8 K splits reduce inside a thread-block cluster (no workspace); more
@@ -48,6 +55,9 @@ bool tc_supported(int dt, int bm, int bn, int N, int K, int M);
 size_t tc_workspace(int dt, int bm, int bn, int N, int K, int M);
 int tc_launches(int dt, int bm);
 cudaError_t launch_tc(const RunArgs& a, int bm, int bn);
+// Tiles whose epilogue can store to peer Y buffers as well (all but the
+// 1-CTA converter-warp A16 kernel).
+bool tc_gather_supported(int dt, int bm);
 
 // Read `bytes` of `buf` (a buffer larger than L2) so that L2 holds only clean
 // lines of it afterwards: a cold cache for the next kernel, without the dirty

@@ -25,7 +25,11 @@ EXPORTS = [
     "gemm_time_e2e", "gemm_time_e2e_pipelined", "gemm_launches_per_run", "gemm_peak_probe",
     "gemm_run_noalloc",
     "gemm_quantize",
+    "gemm_run_gather", "gemm_gather_supported", "gemm_peer_alloc", "gemm_peer_open", "gemm_peer_close",
 ]
+
+MAX_PEERS = 7            # GEMM_MAX_PEERS
+PEER_HANDLE_BYTES = 64   # GEMM_PEER_HANDLE_BYTES
 
 # quantiser formats (GEMM_Q_* in include/mlpgemm.h)
 Q_E4M3_REF, Q_E4M3, Q_E2M1, Q_MXFP4, Q_MXFP8 = 0, 1, 2, 3, 4
@@ -89,6 +93,12 @@ def _declare(L):
         "gemm_run_noalloc": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp,
                                      vp]),
         "gemm_quantize": (c_int, [c_int, c_int, vp, vp, vp, ctypes.c_long, ctypes.c_long, vp]),
+        "gemm_run_gather": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp, vp,
+                                    c_size, vpp, c_int, vp]),
+        "gemm_gather_supported": (c_int, [c_int, c_int]),
+        "gemm_peer_alloc": (c_int, [c_int, c_size, vpp, vp]),
+        "gemm_peer_open": (c_int, [c_int, vp, vpp]),
+        "gemm_peer_close": (c_int, [c_int, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -240,6 +250,44 @@ def run_noalloc(device, dtype, ksplit, X, W, Y, N, K, M, xscale=None, wscale=Non
     check(lib().gemm_run_noalloc(device, dtype, ksplit, as_ptr(X), as_ptr(W), as_ptr(Y), N, K, M,
                                  as_ptr(xscale), as_ptr(wscale), as_ptr(stream)),
           "gemm_run_noalloc")
+
+
+def run_gather(device, dtype, tile, X, W, Y, N, K, M, xscale=None, wscale=None, workspace=None,
+               workspace_bytes=0, peers=(), stream=None) -> None:
+    """gemm_run whose epilogue also stores Y at the same offset from every
+    pointer of `peers` (other GPUs' Y buffers mapped with peer_open)."""
+    arr = (ctypes.c_void_p * max(1, len(peers)))(*[as_ptr(q) for q in peers])
+    check(lib().gemm_run_gather(device, dtype, tile, as_ptr(X), as_ptr(W), as_ptr(Y), N, K, M,
+                                as_ptr(xscale), as_ptr(wscale), as_ptr(workspace), int(workspace_bytes),
+                                arr, len(peers), as_ptr(stream)), "gemm_run_gather")
+
+
+def gather_supported(dtype: int, tile: int) -> bool:
+    return bool(lib().gemm_gather_supported(dtype, tile))
+
+
+def peer_alloc(device: int, nbytes: int):
+    """(device pointer, IPC handle bytes) of a buffer other processes can map."""
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
+    check(lib().gemm_peer_alloc(device, int(nbytes), ctypes.byref(ptr), h), "gemm_peer_alloc")
+    return int(ptr.value), bytes(h.raw)
+
+
+def peer_open(device: int, handle: bytes) -> int:
+    assert len(handle) == PEER_HANDLE_BYTES
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(bytes(handle), PEER_HANDLE_BYTES)
+    check(lib().gemm_peer_open(device, h, ctypes.byref(ptr)), "gemm_peer_open")
+    return int(ptr.value)
+
+
+def peer_close(device: int, ptr: int) -> None:
+    check(lib().gemm_peer_close(device, ctypes.c_void_p(ptr)), "gemm_peer_close")
+
+
+def free(device: int, ptr: int) -> None:
+    check(lib().gemm_free(device, ctypes.c_void_p(ptr)), "gemm_free")
 
 
 def sync(device: int = 0, stream=None) -> None:

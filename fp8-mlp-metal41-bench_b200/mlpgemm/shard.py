@@ -30,7 +30,10 @@ no exchange inside it:
 (generated on rank 0, broadcast once), X rows are dealt out block-cyclically
 (row_blocks), and every rank's block of Y already sits at its final rows, so
 the all-gather is in place into Y[N,M] with no permute, and each round of
-the pipeline gathers straight into Y as well.
+the pipeline gathers straight into Y as well.  With --allgather it also
+times the fused form (`fused_ms`): gemm_run_gather, whose epilogue stores
+each Y tile into every GPU's Y over NVLink (IPC-mapped peer buffers, PeerY),
+followed only by a 1-element all-reduce that orders the GPUs.
 
 torch.distributed is plumbing here (device buffers, NCCL, barriers); the
 GEMM itself is libgemm.so through its C ABI.
@@ -240,7 +243,7 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
         rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
                         rel, gpus=world, allgather_ms=ag_ms))
         extra.append((shape.name, dtype, world, bcast_ms, ag_ms, f"{width}c", med_max * 1000.0,
-                      extra_pipe.get(dtype)))
+                      extra_pipe.get(dtype), None))
     return rows, extra
 
 
@@ -345,7 +348,10 @@ def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
         r0, h = blocks[rank][0]
         xrow = F.x_bytes(dtype, 1, K)
         srow = K // 32 if dtype in F.X_SCALED else 0
-        tile = choose_tile(a, profile, dtype, max(h, 1), K, M)
+        # one tile for every rank (chosen for ch rows), unless it cannot take this rank's rows
+        tile = choose_tile(a, profile, dtype, ch, K, M)
+        if h > 0 and not G.tile_supported(dt, G.tile_index(tile), h, K, M):
+            tile = choose_tile(a, profile, dtype, h, K, M)
         ti = G.tile_index(tile)
         # W: generated on rank 0 and broadcast (timed); X rows: this rank's own
         Wh = ops.W(dtype).view(np.uint8).reshape(-1)
@@ -385,7 +391,7 @@ def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
         r = torch.tensor([rel], dtype=torch.float64, device=dev)
         dist.all_reduce(r, op=dist.ReduceOp.MAX)
         rel = float(r.item())
-        ag_ms = pipe_ms = None
+        ag_ms = pipe_ms = fused_ms = None
         if a.allgather:
             times = []
             for _ in range(6):   # one warm-up, then the median of 5
@@ -403,11 +409,103 @@ def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
             pts = sample_points(N, M, bm, bn) + [(b[0][0], M - 1) for b in blocks if b[0][1]]
             check_samples(ops, dtype, _RowsAt(Y, {n for n, _ in pts}), pts, shape.name)
             pipe_ms = _pipeline_rows(a, torch, dist, world, rank, local, ops, dtype, dt, tile, Wt, WS, Y[:N])
+            # the fused gather runs only if every rank's tile has it (a collective decision)
+            can = torch.tensor([1 if G.gather_supported(dt, ti) or h == 0 else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(can, op=dist.ReduceOp.MIN)
+            if int(can.item()) == 1 and world - 1 <= G.MAX_PEERS:
+                fused_ms = _fused_rows(torch, dist, world, rank, local, dt, ti, Xr, Wt, XS, WS, WSP, wsb, Y[:N],
+                                       K, ch, rounds, h)
         vs = "1.000" if dtype == "fp16" else ("%.3f" % (medians["fp16"] / med_max) if "fp16" in medians else "-")
         rows.append(Row(shape.name, N, K, M, dtype, tile, med_max * 1000.0, flops / med_max / 1e12, vs,
                         rel, gpus=world, allgather_ms=ag_ms))
-        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, f"{ch}r", med_max * 1000.0, pipe_ms))
+        extra.append((shape.name, dtype, world, bcast_ms, ag_ms, f"{ch}r", med_max * 1000.0, pipe_ms, fused_ms))
     return rows, extra
+
+
+class _DevArray:
+    """A zero-copy torch view of a raw device pointer (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+class PeerY:
+    """One IPC-shareable Y buffer per rank, mapped into every other rank.
+
+    `ptrs[g]` is rank g's buffer as seen from this device (this rank's own
+    allocation at g == rank). Collective: every rank constructs and closes
+    it at the same point."""
+
+    def __init__(self, torch, dist, world, rank, local, nbytes: int):
+        self.torch, self.dist, self.world, self.rank, self.local = torch, dist, world, rank, local
+        self.own, handle = G.peer_alloc(local, nbytes)
+        dev = torch.device("cuda", local)
+        mine = torch.tensor(list(handle), dtype=torch.uint8, device=dev)
+        allh = torch.empty(world * G.PEER_HANDLE_BYTES, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(allh, mine)
+        hs = allh.view(world, G.PEER_HANDLE_BYTES).cpu().numpy()
+        self.ptrs = [self.own if g == rank else G.peer_open(local, bytes(hs[g])) for g in range(world)]
+
+    def tensor(self, rows: int, cols: int, dtype):
+        ts = {"float32": "<f4", "int32": "<i4"}[str(dtype).split(".")[-1]]
+        return self.torch.as_tensor(_DevArray(self.own, (rows, cols), ts), device=f"cuda:{self.local}")
+
+    def close(self):
+        self.torch.cuda.synchronize()
+        self.dist.barrier()
+        for g, p in enumerate(self.ptrs):
+            if g != self.rank:
+                G.peer_close(self.local, p)
+        self.dist.barrier()
+        G.free(self.local, self.own)
+
+
+def _fused_rows(torch, dist, world, rank, local, dt, ti, Xr, Wt, XS, WS, WSP, wsb, Yref, K, ch, rounds, h,
+                reps=6):
+    """GEMM whose epilogue also writes this rank's rows into every peer's Y
+    (gemm_run_gather), then a 1-element all-reduce on the same stream that
+    orders every rank after all the peers' writes. Returns the median over
+    reps of the max over ranks of that time (ms), after checking that the
+    Y it leaves on this GPU equals the NCCL-gathered `Yref` bit for bit."""
+    M = Yref.shape[1]
+    dev = torch.device("cuda", local)
+    es = Yref.element_size()
+    peer = PeerY(torch, dist, world, rank, local, rounds * world * ch * M * es)
+    try:
+        Yf = peer.tensor(rounds * world * ch, M, Yref.dtype)
+        Yf.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        off = rank * ch * M * es
+        others = [p + off for g, p in enumerate(peer.ptrs) if g != rank]
+        s = torch.cuda.Stream(device=dev)
+        flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        times = []
+        for _ in range(reps + 1):
+            s.wait_stream(torch.cuda.current_stream(dev))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(s):
+                e0.record(s)
+                if h > 0:
+                    G.run_gather(local, dt, ti, Xr, Wt, peer.own + off, h, K, M, xscale=XS, wscale=WS,
+                                 workspace=WSP, workspace_bytes=wsb, peers=others, stream=s.cuda_stream)
+                dist.all_reduce(flag)
+                e1.record(s)
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1))
+        N = Yref.shape[0]
+        same = bool(torch.equal(Yf[:N], Yref))
+        ok = torch.tensor([1 if same else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) != 1:
+            raise BenchExit(3, "fused all-gather: Y differs from the NCCL-gathered Y")
+        med = sorted(times[1:])[len(times[1:]) // 2]
+        t = torch.tensor([med], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    finally:
+        peer.close()
 
 
 def _pipeline_rows(a, torch, dist, world, rank, local, ops, dtype, dt, tile, Wt, WS, Yref, chunks=4, reps=5):
@@ -517,14 +615,15 @@ def main_sharded(a, shapes) -> int:
         print("")
         hdr = " ".join([_c("shape", 8), _c("dtype", 9), _c("gpus", 4, True), _c("block/gpu", 9, True),
                         _c("bcast_ms", 10, True), _c("allgather_ms", 12, True),
-                        _c("gemm+ag_ms", 11, True), _c("pipeline_ms", 11, True)])
+                        _c("gemm+ag_ms", 11, True), _c("pipeline_ms", 11, True), _c("fused_ms", 9, True)])
         print(hdr)
         print("-" * len(hdr))
-        for (sh, d, g, b, ag, w, gm, pp) in extra:
+        for (sh, d, g, b, ag, w, gm, pp, fu) in extra:
             seq = "-" if ag is None else "%.4f" % (gm + ag)
             print(" ".join([_c(sh, 8), _c(d, 9), _c(str(g), 4, True), _c(w, 9, True),
                             _c("%.4f" % b, 10, True), _c("-" if ag is None else "%.4f" % ag, 12, True),
-                            _c(seq, 11, True), _c("-" if pp is None else "%.4f" % pp, 11, True)]))
+                            _c(seq, 11, True), _c("-" if pp is None else "%.4f" % pp, 11, True),
+                            _c("-" if fu is None else "%.4f" % fu, 9, True)]))
         print("ok")
         sys.stdout.flush()
     return 0

@@ -134,6 +134,36 @@ int gemm_run(int device, int dtype, int tile, const void *X, const void *W, void
              int N, int K, int M, const void *xscale, const void *wscale,
              void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- fused GEMM + all-gather over NVLink (multi-GPU; no reference analogue:
+ * the reference is single-device, main.swift:272) ------------------------------
+ *
+ * gemm_run_gather is gemm_run whose tensor-core epilogue also writes every Y
+ * element at the same byte offset from each of `npeers` peer pointers: the
+ * Y buffers of the other GPUs, mapped into this device with gemm_peer_open.
+ * With rows of X split across GPUs and every GPU's block at its own rows
+ * of a full-size Y, one call per GPU leaves the whole Y on every GPU: the
+ * all-gather happens inside the GEMM, tile by tile, with no collective
+ * launch.  The peers' writes into this GPU's Y are complete once every
+ * GPU's call has finished on its stream (synchronise the GPUs after the
+ * calls, e.g. with a small all-reduce on the same stream).
+ * npeers 0 is gemm_run.  Tensor-core tiles only, except the 1-CTA tiles of
+ * the A16 kinds (int8, fp8, mxfp4 at 128x256 / 128x128): gemm_gather_supported.
+ * Peer pointers must be 16-byte aligned. */
+#define GEMM_MAX_PEERS 7
+#define GEMM_PEER_HANDLE_BYTES 64
+int gemm_run_gather(int device, int dtype, int tile, const void *X, const void *W, void *Y,
+                    int N, int K, int M, const void *xscale, const void *wscale,
+                    void *workspace, size_t workspace_bytes, void *const *ypeers, int npeers,
+                    void *stream);
+int gemm_gather_supported(int dtype, int tile);
+/* Device memory that other processes can map: *ptr gets the allocation (free
+ * it with gemm_free) and `handle` its GEMM_PEER_HANDLE_BYTES-byte IPC handle. */
+int gemm_peer_alloc(int device, size_t bytes, void **ptr, void *handle);
+/* Map another process's gemm_peer_alloc buffer into `device`; unmap with
+ * gemm_peer_close. */
+int gemm_peer_open(int device, const void *handle, void **ptr);
+int gemm_peer_close(int device, void *ptr);
+
 /* Wait for all work on `stream` and check the device error word (timeouts of
  * bounded waits).  The cb.waitUntilCompleted + status check of
  * main.swift:513-518. */

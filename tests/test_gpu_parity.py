@@ -326,3 +326,61 @@ def test_pair_tiles_many_waves(gemm, dtype, shape):
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
     ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), None, None, N, K, M)
     assert_close(dtype, outs[1], ref)
+
+
+GATHER_CASES = [(d, t) for d, t in TC_CASES if not (t != "256x256" and d in ("int8", "fp8", "mxfp4"))]
+
+
+@pytest.mark.parametrize("dtype,tile", GATHER_CASES)
+def test_gather_epilogue_writes_every_peer(gemm, dtype, tile):
+    """gemm_run_gather with seven 'peer' Y buffers on the same GPU: every
+    peer gets exactly the local Y, and the local Y is the oracle's result.
+    (The multi-GPU form maps other GPUs' buffers; the stores are the same.)"""
+    G = gemm
+    N, K, M = 200, 384, 272
+    ops = Operands(N, K, M, "seeded", 3)
+    dt, ti = F.CODE[dtype], G.tile_index(tile)
+    assert G.gather_supported(dt, ti)
+    X = G.DeviceBuffer(0, ops.X(dtype).nbytes).upload(ops.X(dtype))
+    W = G.DeviceBuffer(0, ops.W(dtype).nbytes).upload(ops.W(dtype))
+    xs, ws = ops.xscale(dtype), ops.wscale(dtype)
+    XS = G.DeviceBuffer(0, xs.nbytes).upload(xs) if xs is not None else None
+    WS = G.DeviceBuffer(0, ws.nbytes).upload(ws) if ws is not None else None
+    Y = G.DeviceBuffer(0, N * M * 4).zero()
+    peers = [G.DeviceBuffer(0, N * M * 4).zero() for _ in range(G.MAX_PEERS)]
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+    G.run_gather(0, dt, ti, X, W, Y, N, K, M, XS, WS, WSP, wsb, peers=peers)
+    G.sync(0)
+    yt = np.int32 if dtype == "i8i8" else np.float32
+    out = np.empty((N, M), dtype=yt)
+    Y.download(out)
+    for p in peers:
+        got = np.empty((N, M), dtype=yt)
+        p.download(got)
+        assert np.array_equal(got.view(np.uint32), out.view(np.uint32))
+    ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), xs, ws, N, K, M)
+    assert_close(dtype, out, ref)
+
+
+def test_gather_rejects_unsupported_tiles(gemm):
+    G = gemm
+    for dtype, tile in (("int8", "128x256"), ("mxfp4", "128x128"), ("fp16", "16x128"), ("fp16", "gemv.k1")):
+        assert not G.gather_supported(F.CODE[dtype], G.tile_index(tile))
+    N, K, M = 8, 256, 256
+    dt, ti = F.CODE["fp16"], G.tile_index("16x128")
+    X = G.DeviceBuffer(0, N * K * 2).zero()
+    W = G.DeviceBuffer(0, K * M * 2).zero()
+    Y = G.DeviceBuffer(0, N * M * 4).zero()
+    P = G.DeviceBuffer(0, N * M * 4).zero()
+    wsb = G.workspace_size(dt, ti, N, K, M)
+    WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+    with pytest.raises(G.GemmError) as e:
+        G.run_gather(0, dt, ti, X, W, Y, N, K, M, None, None, WSP, wsb, peers=[P])
+    assert e.value.code == 1 and "fused all-gather" in str(e.value)
+    N = M = K = 256   # a shape the pair tile takes, with more peers than an 8-GPU node has
+    X2, W2 = G.DeviceBuffer(0, N * K * 2).zero(), G.DeviceBuffer(0, K * M * 2).zero()
+    Y2, P2 = G.DeviceBuffer(0, N * M * 4).zero(), G.DeviceBuffer(0, N * M * 4).zero()
+    with pytest.raises(G.GemmError) as e:
+        G.run_gather(0, dt, G.tile_index("256x256"), X2, W2, Y2, N, K, M, None, None, None, 0, peers=[P2] * 8)
+    assert e.value.code == 1 and "npeers" in str(e.value)
