@@ -263,8 +263,10 @@ __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb
 // being stored.
 //
 // With peers (the fused all-gather), each chunk is stored again at the same
-// offset (`yoff`, the row's start) in every peer's Y over NVLink; the stores
-// are plain posted writes, made visible to the peers by the kernel's end.
+// offset in every peer's Y over NVLink; the stores are plain posted writes,
+// made visible to the peers by the kernel's end.  Over NVLink every store
+// instruction should write whole 128-byte lines, not 16 bytes in each of 32
+// rows, so the warp first rearranges the chunk with shuffles (peer_layout).
 __device__ __forceinline__ void store_chunk(uint32_t* yrow, const uint32_t (&r)[32], int cb, int M, bool vec_ok) {
   if (vec_ok && cb + 32 <= M) {
     uint4* dst = reinterpret_cast<uint4*>(yrow + cb);
@@ -277,14 +279,65 @@ __device__ __forceinline__ void store_chunk(uint32_t* yrow, const uint32_t (&r)[
   }
 }
 
+// A 32 x 32 chunk held one row per lane (r[v] = column v of row `lane`) is
+// rearranged so that register group j of lane L holds columns 4(L>>2) ..
+// 4(L>>2)+3 of row 4j + (L&3): three butterfly stages, each swapping one bit
+// of the register group index (k) with lane bit k+2.  Afterwards each group
+// of 8 lanes with the same L&3 covers one row's 128 bytes.
+__device__ __forceinline__ void peer_layout(uint32_t (&r)[32], int lane) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int m = 1 << (k + 2);
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      if (g & (1 << k)) continue;
+      const int gb = g | (1 << k);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t send = hi ? r[4 * g + e] : r[4 * gb + e];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, m);
+        if (hi) r[4 * g + e] = recv;
+        else r[4 * gb + e] = recv;
+      }
+    }
+  }
+}
+
+// Peer stores of one chunk (whole warp): rows row0 .. row0+31 of Y, columns
+// cb .. cb+31, rows at or past N skipped.
+__device__ __forceinline__ void store_peers(uint32_t (&r)[32], const TcParams& p, int row0, int cb, int M,
+                                            bool vec_ok, bool row_ok) {
+  const int lane = (int)(threadIdx.x & 31u);
+  if (!vec_ok) {   // rows of M % 4 floats are not 16-byte aligned: one lane per row
+    if (!row_ok) return;
+#pragma unroll
+    for (int i = 0; i < kMaxPeers; ++i)
+      if (i < p.npeers) store_chunk(p.peer[i] + (size_t)(row0 + lane) * M, r, cb, M, false);
+    return;
+  }
+  peer_layout(r, lane);
+  const int col = cb + 4 * (lane >> 2);
+  if (col >= M) return;   // M % 4 == 0: a group is all in or all out
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int row = row0 + ((j << 2) | (lane & 3));
+    if (row >= p.N) continue;
+    const uint4 v = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+    const size_t off = (size_t)row * M + col;
+#pragma unroll
+    for (int i = 0; i < kMaxPeers; ++i)
+      if (i < p.npeers) *reinterpret_cast<uint4*>(p.peer[i] + off) = v;
+  }
+}
+
 template <int NCH, typename Release>
 __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, int col0, int M, bool row_ok,
-                                               const int8_t* col_exp, const TcParams& p, size_t yoff,
+                                               const int8_t* col_exp, const TcParams& p, int row0,
                                                Release release) {
   const bool vec_ok = (M % 4) == 0;
-  auto store = [&](uint32_t (&r)[32], int c) {
-    const int cb = col0 + c * 32;
-    if (!row_ok) return;
+  // this lane's row: column exponents (if any), then the local store
+  auto store_row = [&](uint32_t (&r)[32], int cb) {
     if (col_exp) {   // f32 results times 2^e per column (exact powers of two)
       // the chunk's 32 exponents in two 16-byte loads (the same for every lane);
       // nothing to do when all are zero, the usual case
@@ -311,11 +364,16 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
       }
     }
     store_chunk(yrow, r, cb, M, vec_ok);
-    if (p.npeers) {
-#pragma unroll
-      for (int i = 0; i < kMaxPeers; ++i)
-        if (i < p.npeers) store_chunk(p.peer[i] + yoff, r, cb, M, vec_ok);
+  };
+  auto store = [&](uint32_t (&r)[32], int c) {
+    const int cb = col0 + c * 32;
+    if (p.npeers) {   // the whole warp takes part in the peer stores
+      if (row_ok) store_row(r, cb);
+      store_peers(r, p, row0, cb, M, vec_ok, row_ok);
+      return;
     }
+    if (!row_ok) return;
+    store_row(r, cb);
   };
   static_assert(NCH % 2 == 0, "chunks come in pairs");
   uint32_t ra[32], rb[32];
@@ -519,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_COLS), yrow, col0,
-                              p.M, row_ok, p.col_exp, p, (size_t)row * p.M, [&] {
+                              p.M, row_ok, p.col_exp, p, row - lane, [&] {
                                 tc_fence_before();
                                 mbar_arrive(&bars->acc_empty[buf]);
                               });
@@ -834,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
       drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN), yrow, col0, p.M,
-                              row_ok, p.col_exp, p, (size_t)row * p.M, [&] {
+                              row_ok, p.col_exp, p, row - lane, [&] {
                                 tc_fence_before();
                                 __syncwarp();
                                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
