@@ -128,6 +128,10 @@ struct TcParams {
   int* dev_err;
   uint32_t* peer[kMaxPeers];   // peer Y bases: every Y store is repeated at the same offset
   int npeers;
+  // CTA-pair kernel work items: tiles 0 .. split_from-1 whole, then every
+  // later tile as two 256 x BN/2 halves (the last, partial wave spread over
+  // twice the pairs); split_from = num_items = the tile count when unsplit
+  int split_from, num_items;
 };
 
 void set_peers(TcParams& p, const RunArgs& a) {
@@ -210,6 +214,19 @@ struct Bars {
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int& tn) {
   tm = tile % tiles_m;
   tn = tile / tiles_m;
+}
+
+// Work item i of the CTA-pair kernel: its tile and, for a half tile, which
+// half of the tile's columns (-1: the whole tile).
+__device__ __forceinline__ void item_coords(int i, const TcParams& p, int& tm, int& tn, int& half) {
+  int t = i;
+  half = -1;
+  if (i >= p.split_from) {
+    const int j = i - p.split_from;
+    t = p.split_from + (j >> 1);
+    half = j & 1;
+  }
+  tile_coords(t, p.tiles_m, tm, tn);
 }
 
 // Scale-factor packing pre-pass.  For every 128-row tile t of an operand,
@@ -706,6 +723,10 @@ struct Cfg2 {
                 ((uint32_t)(256 >> 4) << 24))
              : ((T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | ((T::b_mn ? 1u : 0u) << 16) |
                 ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24));
+  // half tiles (256 x BN/2): unscaled kinds without 4-bit unpacking
+  static constexpr bool HALVES = !SCALED && !A_UNPACK && !B_UNPACK && (!T::b_mn || (BH / 2) % B_BOX_MN == 0);
+  static constexpr int STAGE_TX_H = A_BYTES + B_BYTES / 2;
+  static constexpr uint32_t IDESC_H = (IDESC & ~(0x3Fu << 17)) | ((uint32_t)(BN / 2 >> 3) << 17);
   static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
   static_assert(!T::b_mn || BH % B_BOX_MN == 0, "W half-tile must be whole swizzle atoms");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -715,7 +736,7 @@ template <int DT, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                        TcParams p) {
+                        const __grid_constant__ CUtensorMap tmBh, TcParams p) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -725,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();             // 0 = leader
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int num_tiles = p.tiles_m * p.tiles_n;          // tiles of 256 x BN
+  const int num_items = C::HALVES ? p.num_items : p.tiles_m * p.tiles_n;   // tiles of 256 x BN (or halves)
   AbortCtl ctl{p.dev_err, &bars->abort_flag};
 
   if (threadIdx.x == 0) {
@@ -769,9 +790,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmSA);
       tma_prefetch_desc(&tmSB);
     }
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-      int tm, tn;
-      tile_coords(tile, p.tiles_m, tm, tn);
+    if constexpr (C::HALVES && !T::b_mn) tma_prefetch_desc(&tmBh);
+    for (int item = pair; item < num_items && ok; item += npairs) {
+      int tm, tn, half;
+      item_coords(item, p, tm, tn, half);
+      if constexpr (!C::HALVES) half = -1;
+      // W columns this CTA loads: BH of the tile, or BH/2 of one half of it
+      const int wcol = tn * BN + (half < 0 ? (int)rank * C::BH : half * (BN / 2) + (int)rank * (C::BH / 2));
+      const uint32_t stx = half < 0 ? tx : (uint32_t)C::STAGE_TX_H;
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&bars->empty[stage], phase ^ 1u, ctl, 0x100 + stage)) { ok = false; break; }
         const uint32_t lfull = mapa_shared(&bars->full[stage], 0);
@@ -780,7 +806,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Only the leader arrives, expecting both CTAs' bytes; the peer's loads
         // just complete their transactions on the leader's barrier (a remote
         // arrive per stage would put a cross-SM round trip in the peer's loop).
-        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * tx);
+        if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * stx);
         // x counts elements of the map: 16-bit or 4-bit (unpacking maps) elements, else bytes
         tma_load_2d_pair(a_dst, &tmA, lfull,
                          kb * ((T::a_bits == 16 || C::A_UNPACK) ? C::K_PER_STAGE : kRowBytes),
@@ -798,13 +824,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if constexpr (T::b_mn) {
+          const int boxes = half < 0 ? C::B_BOXES : C::B_BOXES / 2;
 #pragma unroll
           for (int j = 0; j < C::B_BOXES; ++j)
-            tma_load_2d_pair(b_dst + j * C::B_BOX_BYTES, &tmB, lfull, tn * BN + (int)rank * C::BH + j * C::B_BOX_MN,
-                             kb * C::K_PER_STAGE);
+            if (j < boxes)
+              tma_load_2d_pair(b_dst + j * C::B_BOX_BYTES, &tmB, lfull, wcol + j * C::B_BOX_MN, kb * C::K_PER_STAGE);
         } else {
-          tma_load_2d_pair(b_dst, &tmB, lfull, kb * (C::B_UNPACK ? C::K_PER_STAGE : kRowBytes),
-                           tn * BN + (int)rank * C::BH);
+          if (half < 0)
+            tma_load_2d_pair(b_dst, &tmB, lfull, kb * (C::B_UNPACK ? C::K_PER_STAGE : kRowBytes), wcol);
+          else   // a half tile: the half-height box of the same rows
+            tma_load_2d_pair(b_dst, &tmBh, lfull, kb * kRowBytes, wcol);
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
@@ -834,12 +863,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++local) {
+    for (int item = pair; item < num_items && ok; item += npairs, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       if (!mbar_wait(&bars->acc_empty[buf], acc_par ^ 1u, ctl, 0x200 + buf)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+      const uint32_t idesc = (C::HALVES && item >= p.split_from) ? C::IDESC_H : C::IDESC;   // N = BN/2 for a half
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&bars->full[stage], phase, ctl, 0x300 + stage)) { ok = false; break; }
         tc_fence_after();
@@ -864,7 +894,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
             const uint64_t adesc = sdesc_sw128(a_addr + kk * C::MMA_K_BYTES, 16, 1024);
             const uint64_t bdesc = sdesc_sw128(b_addr + kk * C::B_ADV, C::B_LBO, 1024);
-            tc_mma_pair<T::kind>(d_tmem, adesc, bdesc, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+            tc_mma_pair<T::kind>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
         }
         tc_commit_pair(&bars->empty[stage], 0x3);
@@ -878,9 +908,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------ epilogue (both CTAs) ----------------------------
     const int q = warp - 4;
     int local = 0;
-    for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
-      int tm, tn;
-      tile_coords(tile, p.tiles_m, tm, tn);
+    for (int item = pair; item < num_items; item += npairs, ++local) {
+      int tm, tn, half;
+      item_coords(item, p, tm, tn, half);
+      if constexpr (!C::HALVES) half = -1;
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
       const bool got = mbar_wait(&bars->acc_full[buf], acc_par, ctl, 0x400 + buf);
@@ -888,15 +919,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       tc_fence_after();
       const int row = tm * 256 + (int)rank * kBM + q * 32 + lane;
-      const int col0 = tn * BN;
+      const int col0 = tn * BN + (half > 0 ? BN / 2 : 0);
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
-      drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN), yrow, col0, p.M,
-                              row_ok, p.col_exp, p, row - lane, [&] {
-                                tc_fence_before();
-                                __syncwarp();
-                                if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
-                              });
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
+      };
+      if (C::HALVES && half >= 0)
+        drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release);
+      else
+        drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release);
     }
   }
 
@@ -1420,6 +1455,7 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   p.dev_err = a.dev_err;
   set_peers(p, a);
   const int tiles = p.tiles_m * p.tiles_n;
+  p.split_from = p.num_items = tiles;   // whole tiles only
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_gemm_kernel<DT, BN, STAGES>;
   static unsigned attr_mask = 0;   // per device: dynamic shared memory opt-in done
@@ -1465,6 +1501,13 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
     ok = make_map(&tmB, W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH);
   }
   if (!ok) return cudaErrorInvalidValue;
+  // half tiles (K-major W): the same rows in boxes of BH/2
+  CUtensorMap tmBh = tmB;
+  if constexpr (C::HALVES && !T::b_mn) {
+    const uint64_t row_bytes = (uint64_t)a.K * T::b_bits / 8;
+    if (!make_map(&tmBh, W, ty8, row_bytes, (uint64_t)a.M, row_bytes, kRowBytes, C::BH / 2))
+      return cudaErrorInvalidValue;
+  }
   // packed scale blocks as 2-D maps: rows of 128 x 32-bit (512 bytes), SF_CELLS rows per box
   tmSA = tmA;
   tmSB = tmA;
@@ -1512,8 +1555,12 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   }
   const int cap = max_pairs[dev & 31] > 0 ? max_pairs[dev & 31] : a.num_sms / 2;
   const int pairs = tiles < cap ? tiles : cap;
+  // a last wave of at most half the pairs runs as twice as many half tiles
+  const int rem = tiles % pairs;
+  p.split_from = (C::HALVES && rem > 0 && 2 * rem <= pairs) ? tiles - rem : tiles;
+  p.num_items = tiles + (tiles - p.split_from);
   cfg.gridDim = dim3(2 * pairs);
-  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, tmSA, tmSB, p);
+  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, tmSA, tmSB, tmBh, p);
 }
 
 template <int DT, int BN, int STAGES>

@@ -302,11 +302,18 @@ def test_f4f4_pair_ragged_m(gemm, M):
     assert_close("f4f4", out, ref)
 
 
-@pytest.mark.parametrize("dtype", ["fp16", "i8i8", "f8f8"])
-@pytest.mark.parametrize("shape", [(256, 256, 19200), (512, 256, 14080)])
+# More 256x256 tiles than CTA pairs: the persistent grid takes several waves.
+# When the last wave fills at most half the pairs, its tiles run as 256x128
+# halves. Cases: 1 and 36 split tiles; a split last tile whose second half is
+# partly (19152) or wholly (19056) past M; 160 tiles over several tile rows
+# with 12 split; int8 through the widened-W pair kernel.
+MANY_WAVES = [(256, 256, 19200), (512, 256, 14080), (256, 256, 19152), (256, 256, 19056), (2048, 256, 5120)]
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "i8i8", "f8f8", "int8"])
+@pytest.mark.parametrize("shape", MANY_WAVES)
 def test_pair_tiles_many_waves(gemm, dtype, shape):
-    # more 256x256 tiles than CTA pairs (75 and 110 tiles: the persistent grid
-    # takes several waves, the last one short); two calls give the same bits
+    # two calls give the same bits, and the result matches the oracle
     G = gemm
     N, K, M = shape
     ops = Operands(N, K, M, "seeded", 8)
@@ -361,6 +368,30 @@ def test_gather_epilogue_writes_every_peer(gemm, dtype, tile):
         assert np.array_equal(got.view(np.uint32), out.view(np.uint32))
     ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), xs, ws, N, K, M)
     assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "i8i8"])
+def test_gather_epilogue_on_half_tiles(gemm, dtype):
+    # 75 tiles on 74 CTA pairs: the last tile runs as two 256x128 halves, whose
+    # second half is partly past M; every peer still gets exactly the local Y
+    G = gemm
+    N, K, M = 256, 256, 19152
+    ops = Operands(N, K, M, "seeded", 5)
+    dt, ti = F.CODE[dtype], G.tile_index("256x256")
+    X = G.DeviceBuffer(0, ops.X(dtype).nbytes).upload(ops.X(dtype))
+    W = G.DeviceBuffer(0, ops.W(dtype).nbytes).upload(ops.W(dtype))
+    Y = G.DeviceBuffer(0, N * M * 4).zero()
+    peers = [G.DeviceBuffer(0, N * M * 4).zero() for _ in range(3)]
+    G.run_gather(0, dt, ti, X, W, Y, N, K, M, None, None, None, 0, peers=peers)
+    G.sync(0)
+    yt = np.int32 if dtype == "i8i8" else np.float32
+    out = np.empty((N, M), dtype=yt)
+    Y.download(out)
+    for q in peers:
+        got = np.empty((N, M), dtype=yt)
+        q.download(got)
+        assert np.array_equal(got.view(np.uint32), out.view(np.uint32))
+    assert_close(dtype, out, oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), None, None, N, K, M))
 
 
 def test_gather_rejects_unsupported_tiles(gemm):
