@@ -39,6 +39,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "formats.cuh"
@@ -202,6 +203,12 @@ struct Cfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
+// Tensor maps of the peers' Y blocks (fused all-gather on CTA pairs): [N, M]
+// of 32-bit words from the peer's base pointer, 32 x 32 boxes, 128-byte swizzle.
+struct PeerMaps {
+  CUtensorMap m[kMaxPeers];
+};
+
 struct Bars {
   uint64_t full[8];
   uint64_t empty[8];
@@ -348,10 +355,39 @@ __device__ __forceinline__ void store_peers(uint32_t (&r)[32], const TcParams& p
   }
 }
 
+// Peer stores of one chunk through the TMA (whole warp): the chunk goes to
+// this warp's 4 KB staging buffer (`epi`, 1024-byte aligned) with the 128-byte
+// swizzle, which keeps the 32 row writes free of bank conflicts, and lane 0
+// stores the 32 x 32 box to every peer's map at (cb, row0).  The next chunk
+// waits until the TMA has read the buffer.
+__device__ __forceinline__ void store_peers_tma(const uint32_t (&r)[32], unsigned char* epi, const PeerMaps* pm,
+                                                int npeers, int row0, int cb, int N, int M) {
+  const int lane = (int)(threadIdx.x & 31u);
+  const uint32_t base = smem_u32(epi);
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    const uint32_t a = base + (uint32_t)lane * 128u + (uint32_t)((v ^ (lane & 7)) << 4);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(r[4 * v]), "r"(r[4 * v + 1]),
+                 "r"(r[4 * v + 2]), "r"(r[4 * v + 3])
+                 : "memory");
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (row0 < N && cb < M) {
+      for (int i = 0; i < npeers; ++i) tma_store_2d(&pm->m[i], base, cb, row0);
+      bulk_commit_group();
+    }
+    bulk_wait_read_all();
+  }
+  __syncwarp();
+}
+
 template <int NCH, typename Release>
 __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, int col0, int M, bool row_ok,
                                                const int8_t* col_exp, const TcParams& p, int row0,
-                                               Release release) {
+                                               Release release, unsigned char* epi = nullptr,
+                                               const PeerMaps* pm = nullptr) {
   const bool vec_ok = (M % 4) == 0;
   // this lane's row: column exponents (if any), then the local store
   auto store_row = [&](uint32_t (&r)[32], int cb) {
@@ -386,7 +422,8 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
     const int cb = col0 + c * 32;
     if (p.npeers) {   // the whole warp takes part in the peer stores
       if (row_ok) store_row(r, cb);
-      store_peers(r, p, row0, cb, M, vec_ok, row_ok);
+      if (epi && vec_ok) store_peers_tma(r, epi, pm, p.npeers, row0, cb, p.N, M);
+      else store_peers(r, p, row0, cb, M, vec_ok, row_ok);
       return;
     }
     if (!row_ok) return;
@@ -717,7 +754,11 @@ struct Cfg2 {
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  // unscaled kinds: 4 KB per epilogue warp to stage peer stores for the TMA
+  static constexpr bool PEER_TMA = !SCALED;
+  static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
+  static constexpr int SMEM_BYTES = (PEER_TMA ? EPI_OFF + 4 * 4096 : BAR_OFF + 256) + 1024;
+  static constexpr int SMEM_BASE = BAR_OFF + 256 + 1024;   // launches without peer stores
   static constexpr uint32_t IDESC =
       SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
                 ((uint32_t)(256 >> 4) << 24))
@@ -736,7 +777,8 @@ template <int DT, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                        const __grid_constant__ CUtensorMap tmBh, TcParams p) {
+                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ PeerMaps pm,
+                        TcParams p) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -928,11 +970,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
       };
+      unsigned char* epi = C::PEER_TMA ? smem + C::EPI_OFF + q * 4096 : nullptr;
       if (C::HALVES && half >= 0)
-        drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release);
+        drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
       else
-        drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release);
+        drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
     }
+    // peer stores still in flight complete before the CTA ends
+    if (C::PEER_TMA && p.npeers && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   if (aborted_any || aborted(ctl)) {
@@ -1559,8 +1605,20 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   const int rem = tiles % pairs;
   p.split_from = (C::HALVES && rem > 0 && 2 * rem <= pairs) ? tiles - rem : tiles;
   p.num_items = tiles + (tiles - p.split_from);
+  // peers' Y blocks as TMA store targets (rows of M 32-bit words, a multiple of 16 bytes)
+  PeerMaps pm;
+  std::memset(&pm, 0, sizeof(pm));
+  const bool use_epi = C::PEER_TMA && a.npeers > 0 && a.M % 4 == 0;
+  // the staging buffers are dynamic shared memory, requested only when used
+  cfg.dynamicSmemBytes = use_epi ? C::SMEM_BYTES : C::SMEM_BASE;
+  if (use_epi) {
+    for (int i = 0; i < a.npeers; ++i)
+      if (!make_map(&pm.m[i], a.ypeers[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, (uint64_t)a.M, (uint64_t)a.N,
+                    (uint64_t)a.M * 4, 32, 32))
+        return cudaErrorInvalidValue;
+  }
   cfg.gridDim = dim3(2 * pairs);
-  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, tmSA, tmSB, tmBh, p);
+  return cudaLaunchKernelEx(&cfg, k, tmA, tmB, tmSA, tmSB, tmBh, pm, p);
 }
 
 template <int DT, int BN, int STAGES>
