@@ -78,3 +78,35 @@ def test_workspace_sizes():
     t = G.tile_index("gemv.k32")
     assert G.workspace_size(F.CODE["int8"], t, 1, 4096, 11008) == 65536 + 32 * 11008 * 4
     assert G.workspace_size(F.CODE["int8"], G.tile_index("gemv.k1"), 1, 4096, 11008) == 0
+
+
+def test_gather_support_table():
+    # the fused all-gather rides on the tensor-core epilogues: every CTA-pair
+    # tile, and the 1-CTA tiles except the converter-warp A16 kernel
+    pair, one = G.tile_index("256x256"), G.tile_index("128x256")
+    for d in F.DTYPES:
+        assert G.gather_supported(F.CODE[d], pair), d
+    for d in ("fp16", "i8i8", "f8f8", "f4f4", "mxfp4/a4", "mxfp4/a8", "mxfp4/f8"):
+        assert G.gather_supported(F.CODE[d], one), d
+    for d in ("int8", "fp8", "mxfp4"):
+        assert not G.gather_supported(F.CODE[d], one), d
+    for t in ("16x128", "gemv.k1", "gemv.k4"):
+        assert not G.gather_supported(F.CODE["fp16"], G.tile_index(t)), t
+    assert not G.gather_supported(99, pair) and not G.gather_supported(0, 999)
+
+
+def test_gather_entry_points_fail_loudly_without_gpu():
+    if G.device_count() > 0:
+        pytest.skip("a GPU is present")
+    L = G.lib()
+    with pytest.raises(G.GemmError) as e:   # no initialised device
+        G.run_gather(0, F.CODE["fp16"], G.tile_index("256x256"), 1 << 20, 1 << 20, 1 << 20, 256, 256, 256,
+                     peers=[1 << 20])
+    assert e.value.code == G.GEMM_ERR_INIT
+    with pytest.raises(G.GemmError):
+        G.peer_alloc(0, 4096)
+    with pytest.raises(G.GemmError):
+        G.peer_open(0, bytes(G.PEER_HANDLE_BYTES))
+    import ctypes
+    assert L.gemm_peer_alloc(0, 16, None, None) == G.GEMM_ERR_ARGS
+    assert L.gemm_peer_open(0, None, ctypes.byref(ctypes.c_void_p())) == G.GEMM_ERR_ARGS

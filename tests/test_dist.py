@@ -137,3 +137,19 @@ def test_two_gloo_ranks_row_shard_gather_in_place():
     mp.spawn(_rows_worker, args=(world, _free_port(), out), nprocs=world, join=True)
     for r in range(world):
         assert all(out[r].values()), out[r]
+
+
+def test_rank_rows_block_cyclic_with_padding():
+    import numpy as np
+    from mlpgemm.shard import _rank_rows, row_blocks
+    N, row_bytes = 1000, 6
+    # 16-bit values, distinct per row, seen as rows of 2 * row_bytes bytes
+    X = (np.arange(N)[:, None] * 7 + np.arange(row_bytes)[None, :]).astype(np.uint16).view(np.uint8)
+    rb = 2 * row_bytes
+    for world, chunks in ((2, 2), (4, 1), (3, 2)):
+        ch, rounds, blocks = row_blocks(N, world, chunks)
+        for g in range(world):
+            out = _rank_rows(X, rb, blocks[g], ch).reshape(rounds, ch, rb)
+            for c, (r0, h) in enumerate(blocks[g]):
+                assert np.array_equal(out[c, :h], X.reshape(N, rb)[r0:r0 + h])
+                assert not out[c, h:].any()   # zero past N
