@@ -42,7 +42,6 @@ from __future__ import annotations
 
 import datetime
 import os
-import statistics
 import sys
 
 import numpy as np
