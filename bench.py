@@ -2,27 +2,45 @@
 """bench.py -- the headline measurement of the B200 MLP GEMM.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--dtype D --N n --K k --M m]
+                    [--dtype D --N n --K k --M m --tile T]
+                    [--no-suite] [--no-gathers] [--no-cpu-baseline]
 
-Workload (default): the i8i8 -> int32 square GEMM, N = K = M = 4096, seeded
-int8 operands U{-127..127}, bit-exact against an int64 dot product.  A step
-is one GEMM.  W untimed warm-up steps, then exactly K timed steps, each
-bracketed by its own CUDA-event pair on the launching stream; a 256 MiB
-buffer (> the 126 MB L2) is read before every timed step, outside the
-event pair, so every step starts with a cold L2 (of clean lines: no dirty
-write-back competes with the timed GEMM).  Under torchrun each
-rank runs its own M-slice of a G-times wider GEMM (weak scaling, no data
-collective); the time is the max over ranks.
+Workload (default): the fat row of the reference's suite, f8f8 (E4M3 x
+E4M3 -> f32), N=2048, K=4096, M=11008, operands RNE-rounded from N(0,1) with
+a fixed seed, M-sharded across the GPUs of the job (strong scaling): X is
+broadcast once over NCCL, rank g computes the columns [m0_g, m0_g + w_g) of
+Y from its column block of W (32-column aligned), and N=1 is the whole GEMM.
+A step is one GEMM on every rank.  W untimed warm-up steps, then exactly K
+timed steps, each between its own CUDA-event pair on the launching stream;
+a 256 MiB buffer (> the 126 MB L2) is read before every timed step, outside
+its events, so every step starts with a cold L2 holding only clean lines.
+The step time of the job is the max over ranks; value = 2*N*K*M per step /
+that time.
 
-One JSON line on rank 0 with value (whole-job TOPS), e2e (the same metric
-through the C ABI from pinned host buffers, copies inside the timed
-region), roofline (the GEMM kernel against the measured peak), cpu_baseline
-(the reference's CPU dot product, re-run as an OpenMP host GEMM on a bounded
-sample), clocks (NVML samples during the timed region) and gpu_launches.
+The JSON line (rank 0) carries, besides the contract's keys:
+  parity     this rank's block checked on whole rows against an fp64 numpy
+             dot product of the decoded operands (max rel <= 1e-3), every rank
+  e2e        the same metric through the C ABI from pinned host buffers: every
+             step copies X in, runs the GEMM and copies the rank's Y block out
+  roofline   the GEMM kernel against the measured peak (MEASURED_PEAKS.json)
+  clocks     NVML SM clock and throttle reasons sampled every 0.5 ms while any
+             timed GPU region runs (warm-up, timed steps and the suite), per rank
+  sharded    (N > 1) the collectives beside the GEMM, timed separately: NCCL
+             broadcast of X, NCCL all-gather of the M-sharded Y + permute, the
+             N-sharded GEMM with its in-place NCCL all-gather, and the fused
+             GEMM + all-gather over NVLink peer stores (gemm_run_gather), whose
+             Y must equal the NCCL-gathered Y bit for bit on every rank
+  suite      (N = 1) all 30 dtype x shape rows of the reference's suite
+             (main.swift:156-160) on their default tiles, cold L2, with time,
+             rate, fraction of the measured per-kind peak (thin row: of HBM),
+             fraction of the tcgen05 probe peak, parity and clocks per row
+  probe      (N = 1) gemm_peak_probe per tcgen05 kind (operands resident in
+             shared memory)
+  cpu_baseline (N = 1) the reference's CPU dot product as an OpenMP host GEMM
 
 --impl reference times the reference's CPU implementation of the path (the
-oracle's restatement of its host dot product, main.swift:563-583) on all host
-cores, for the same workload and metric.
+oracle's restatement of its host dot product, main.swift:577-583) on all host
+cores, for the same workload, metric and config (rank 0 only).
 """
 from __future__ import annotations
 
@@ -44,20 +62,26 @@ import numpy as np  # noqa: E402
 
 FLUSH_BYTES = 256 << 20
 BASELINE_METRIC = "TFLOPS/TOPS per dtype×shape at 1/2/4/8 B200; % of tensor-peak or HBM roofline"
+# the reference's suite shapes (main.swift:156-160); iterations per suite row
+SUITE = [("square", 4096, 4096, 4096, 20), ("fat", 2048, 4096, 11008, 20), ("thin", 1, 4096, 11008, 50)]
+KIND_RATIO = {"f16": 1.0, "i8": 2.0, "f8f6f4": 2.0, "mxf4": 4.0}
+PROBE_KIND = {"f16": 0, "i8": 1, "f8f6f4": 2, "mxf8f6f4": 3, "mxf4": 4}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--dtype", default="i8i8")
-    ap.add_argument("--N", type=int, default=4096)
+    ap.add_argument("--dtype", default="f8f8")
+    ap.add_argument("--N", type=int, default=2048)
     ap.add_argument("--K", type=int, default=4096)
-    ap.add_argument("--M", type=int, default=4096)
+    ap.add_argument("--M", type=int, default=11008)
     ap.add_argument("--tile", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-suite", action="store_true")
+    ap.add_argument("--no-gathers", action="store_true")
     return ap.parse_args()
 
 
@@ -72,10 +96,33 @@ def unit_of(dtype):
     return "TOPS" if dtype == "i8i8" else "TFLOPS"
 
 
-def workload_name(dtype, N, K, M):
-    sq = N == K == M
-    shape = "square" if sq else ("thin" if N == 1 else "custom")
-    return f"{dtype} {shape} GEMM N={N} K={K} M={M}"
+def shape_name(N, K, M):
+    for name, n, k, m, _ in SUITE:
+        if (n, k, m) == (N, K, M):
+            return name
+    return "custom"
+
+
+OPERANDS = {
+    "fp16": "X, W half U[-1,1]", "int8": "X half N(0,1), W int8 U{-127..127}",
+    "i8i8": "X, W int8 U{-127..127}", "fp8": "X half N(0,1), W RNE_E4M3(N(0,1))",
+    "f8f8": "X, W RNE_E4M3(N(0,1))", "f4f4": "X, W E2M1 codes U{0..15} (unscaled)",
+    "mxfp4": "X half N(0,1), W E2M1 U{0..15} [M,K] with UE8M0 U{124..130} per 32",
+    "mxfp4/a4": "X, W E2M1 U{0..15} with UE8M0 U{124..130} per 32, W [M,K]",
+    "mxfp4/a8": "X RNE_E4M3(N(0,1)) with UE8M0 U{124..130} per 32, W E2M1 [M,K] with UE8M0",
+    "mxfp4/f8": "X RNE_E4M3(N(0,1)), W E2M1 [M,K] with UE8M0 U{124..130} per 32",
+}
+
+
+def workload_config(dtype, N, K, M, world):
+    """The workload, identical in both arms (no arm-specific keys)."""
+    return {"workload": f"{dtype} {shape_name(N, K, M)} GEMM N={N} K={K} M={M}, M-sharded across {world} GPU(s)",
+            "dtype": dtype, "N": N, "K": K, "M": M, "gpus": world,
+            "operands": f"seeded i.i.d.: {OPERANDS.get(dtype, 'seeded')} (numpy PCG64, seed 0)",
+            "accumulate": "int32" if dtype == "i8i8" else "f32",
+            "sharding": "W column blocks of 32-column multiples per GPU, X replicated (NCCL broadcast once); "
+                        "strong scaling: the same GEMM at every GPU count",
+            "l2": "flushed: a 256 MiB buffer is read before every timed step, outside its events"}
 
 
 def peaks():
@@ -93,20 +140,33 @@ def peaks():
     return hbm, bf16, src
 
 
-KIND_RATIO = {"f16": 1.0, "i8": 2.0, "f8f6f4": 2.0, "mxf4": 4.0}
+def nvml_index(local):
+    """NVML index of CUDA device `local` (CUDA_VISIBLE_DEVICES may renumber)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+               "applications_clocks_setting": 0x2, "sync_boost": 0x10}
 
 
 class ClockSampler:
-    """NVML SM clock / throttle-reason samples while the timed region runs."""
+    """NVML SM clock and throttle reasons, polled every 0.5 ms by a thread
+    that keeps a sample only while a timed GPU region is open (`window`)."""
 
     def __init__(self, index):
         self.index = index
-        self.samples = []
-        self.reasons = set()
+        self.samples = []        # (sm_mhz, reason bits)
+        self.active = False
         self.max_mhz = None
+        self.err = None
         self._stop = threading.Event()
         self._t = None
-        self.err = None
 
     def __enter__(self):
         try:
@@ -124,26 +184,15 @@ class ClockSampler:
 
     def _run(self):
         N = self._N
-        names = {
-            "gpu_idle": getattr(N, "nvmlClocksEventReasonGpuIdle", 0x1),
-            "applications_clocks_setting": getattr(N, "nvmlClocksEventReasonApplicationsClocksSetting", 0x2),
-            "sw_power_cap": getattr(N, "nvmlClocksEventReasonSwPowerCap", 0x4),
-            "hw_slowdown": getattr(N, "nvmlClocksEventReasonHwSlowdown", 0x8),
-            "sync_boost": getattr(N, "nvmlClocksEventReasonSyncBoost", 0x10),
-            "sw_thermal_slowdown": getattr(N, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
-            "hw_thermal_slowdown": getattr(N, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
-            "hw_power_brake_slowdown": getattr(N, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
-        }
         while not self._stop.is_set():
-            try:
-                self.samples.append(N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM))
-                r = N.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                for k, bit in names.items():
-                    if r & bit and k != "gpu_idle":
-                        self.reasons.add(k)
-            except Exception as e:
-                self.err = str(e)
-                break
+            if self.active:
+                try:
+                    mhz = N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM)
+                    bits = N.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                    self.samples.append((mhz, bits))
+                except Exception as e:
+                    self.err = str(e)
+                    break
             time.sleep(0.0005)
 
     def __exit__(self, *a):
@@ -151,10 +200,33 @@ class ClockSampler:
         if self._t:
             self._t.join(timeout=2)
 
-    def summary(self):
-        d = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
-             "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-             "samples": len(self.samples), "source": "nvml, polled every 0.5 ms during the timed steps"}
+    class _Window:
+        def __init__(self, clk):
+            self.clk = clk
+
+        def __enter__(self):
+            self.i0 = len(self.clk.samples)
+            self.clk.active = True
+            return self
+
+        def __exit__(self, *a):
+            self.clk.active = False
+            self.i1 = len(self.clk.samples)
+
+        def summary(self):
+            return self.clk.summary(self.i0, self.i1)
+
+    def window(self):
+        return ClockSampler._Window(self)
+
+    def summary(self, i0=0, i1=None):
+        s = self.samples[i0:i1]
+        bits = 0
+        for _, b in s:
+            bits |= b
+        d = {"sm_mhz": statistics.median([m for m, _ in s]) if s else None,
+             "sm_min_mhz": min((m for m, _ in s), default=None), "sm_max_mhz": self.max_mhz,
+             "reasons": sorted(k for k, v in REASON_BITS.items() if bits & v), "samples": len(s)}
         if self.err:
             d["error"] = self.err
         return d
@@ -163,34 +235,36 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------
 # CPU side: the reference's CPU dot product as a multithreaded host GEMM
 # ---------------------------------------------------------------------------------
-def cpu_sample(dtype, N, K, M, seconds, seed=0):
-    """Time the oracle's host GEMM on rows of the same workload for about
-    `seconds`; returns (TOPS-or-TFLOPS, rows, threads, elapsed)."""
+def _cpu_gemm(dtype, ops):
     import oracle
-    from mlpgemm import formats as F
-    from mlpgemm.data import Operands
-    ops = Operands(N, K, M, "seeded", seed)
+    N, K, M = ops.N, ops.K, ops.M
     threads = oracle.num_threads()
     if dtype == "i8i8":
         X, W = ops.X(dtype), ops.W(dtype)
 
-        def go(r0, nr):
-            return oracle.host_gemm_i32(X, W, K, M, r0, nr, threads)
+        def go(nr):
+            return oracle.host_gemm_i32(X, W, K, M, 0, nr, threads)
     else:
         xf = oracle.decode_x(dtype, ops.X(dtype), ops.xscale(dtype), N, K).astype(np.float32)
         wf = oracle.decode_w(dtype, ops.W(dtype), ops.wscale(dtype), K, M).astype(np.float32)
 
-        def go(r0, nr):
-            return oracle.host_gemm_f32(xf, wf, r0, nr, threads)
-    del F
-    # calibrate on a few rows, then size the sample to ~`seconds`
+        def go(nr):
+            return oracle.host_gemm_f32(xf, wf, 0, nr, threads)
+    return go, threads
+
+
+def cpu_sample(dtype, ops, seconds):
+    """The oracle's host GEMM on output rows of the same workload for about
+    `seconds`; returns (rate, rows, threads, elapsed)."""
+    go, threads = _cpu_gemm(dtype, ops)
+    N, K, M = ops.N, ops.K, ops.M
     nr = min(N, 4)
     t0 = time.perf_counter()
-    go(0, nr)
+    go(nr)
     dt = max(time.perf_counter() - t0, 1e-4)
     rows = int(max(1, min(N, nr * seconds / dt)))
     t0 = time.perf_counter()
-    go(0, rows)
+    go(rows)
     el = time.perf_counter() - t0
     return 2.0 * rows * K * M / el / 1e12, rows, threads, el
 
@@ -199,74 +273,219 @@ def reference_arm(a):
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    dtype, N, K, M = a.dtype, a.N, a.K, a.M
-    import oracle
     from mlpgemm.data import Operands
+    dtype, N, K, M = a.dtype, a.N, a.K, a.M
     ops = Operands(N, K, M, "seeded", 0)
-    threads = oracle.num_threads()
-    X, W = ops.X(dtype), ops.W(dtype)
-    if dtype != "i8i8":
-        xf = oracle.decode_x(dtype, X, ops.xscale(dtype), N, K).astype(np.float32)
-        wf = oracle.decode_w(dtype, W, ops.wscale(dtype), K, M).astype(np.float32)
-
-    def step(nr):
-        if dtype == "i8i8":
-            oracle.host_gemm_i32(X, W, K, M, 0, nr, threads)
-        else:
-            oracle.host_gemm_f32(xf, wf, 0, nr, threads)
-
-    # rows per step: ~1 s of work, so warmup + steps stays within a few minutes
+    go, threads = _cpu_gemm(dtype, ops)
+    # rows per step: about 1 s of work, so warm-up + steps stays within a few minutes
     t0 = time.perf_counter()
-    step(min(N, 4))
+    go(min(N, 4))
     dt = max(time.perf_counter() - t0, 1e-4)
     budget = max(0.05, min(1.0, 150.0 / max(1, a.steps + a.warmup)))
     rows = int(max(1, min(N, min(N, 4) * budget / dt)))
     for _ in range(a.warmup):
-        step(rows)
+        go(rows)
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        step(rows)
+        go(rows)
     el = time.perf_counter() - t0
     v = 2.0 * rows * K * M * a.steps / el / 1e12
     unit = unit_of(dtype)
-    sample = f"{rows} of {N} output rows per step (all {M} columns, K={K}), OpenMP over {threads} threads"
+    sample = (f"{rows} of {N} output rows per step (all {M} columns, K={K}): the reference's host dot "
+              f"product (main.swift:577-583) as an OpenMP host GEMM over {threads} threads "
+              f"(oracle/mlp_oracle.c), on rank 0 only")
     line = {
         "impl": "reference", "metric": BASELINE_METRIC, "value": v, "unit": unit,
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": el / a.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8" if dtype == "i8i8" else "f32", "data": "synthetic",
-        "config": {"workload": workload_name(dtype, N, K, M), "N": N, "K": K, "M": M,
-                   "impl_detail": "the reference's host dot product (main.swift:563-583) run as a "
-                                  "multithreaded host GEMM (oracle/mlp_oracle.c)"},
+        "config": workload_config(dtype, N, K, M, world),
         "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
+    sys.stdout.flush()
     return 0
 
 
 # ---------------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------------
-def traffic_for(kernel_key):
+def traffic_for(key):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(path) as f:
             t = json.load(f)
-        return t.get(kernel_key, {}).get("dram_bytes_per_launch")
+        return t.get(key)
     except (OSError, ValueError):
         return None
+
+
+def check_rows_of(ops, dtype, Yhost, rows, m0, width, wdec=None):
+    """Whole rows [rows, m0:m0+width] of Y against an fp64 numpy dot product of
+    the decoded operands (mlpgemm.data).  i8i8 bit-exact, float dtypes
+    max rel <= 1e-3 (denominator max(|ref|, 1e-2 rms)).  Returns (ok, max rel)."""
+    ref = ops.x_rows(dtype, rows) @ (wdec if wdec is not None else ops.w_cols(dtype, np.arange(m0, m0 + width)))
+    got = Yhost[rows].astype(np.float64)
+    if dtype == "i8i8":
+        return bool(np.array_equal(got, ref)), 0.0
+    if not np.all(np.isfinite(got)):
+        return False, float("inf")
+    rms = float(np.sqrt(np.mean(ref * ref)))
+    rel = float(np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-2 * rms + 1e-30)))
+    return rel <= 1e-3, rel
+
+
+def parity_rows(N):
+    return sorted({0, min(N - 1, 127), min(N - 1, 128), min(N - 1, 255), min(N - 1, 256), N // 2, N - 1})
+
+
+class Dev:
+    """Device buffers of one rank: DeviceBuffer (gemm_alloc) on one GPU,
+    torch tensors under torchrun (NCCL needs them)."""
+
+    def __init__(self, G, local, torch=None):
+        self.G, self.local, self.torch = G, local, torch
+        self.keep = []
+
+    def empty(self, nbytes):
+        if self.torch is None:
+            b = self.G.DeviceBuffer(self.local, max(1, nbytes))
+        else:
+            b = self.torch.empty(max(1, nbytes), dtype=self.torch.uint8, device=f"cuda:{self.local}")
+        self.keep.append(b)
+        return b
+
+    def zeros(self, nbytes):
+        b = self.empty(nbytes)
+        if self.torch is None:
+            b.zero()
+        else:
+            b.zero_()
+        return b
+
+    def upload(self, arr):
+        if arr is None:
+            return None
+        if self.torch is None:
+            b = self.G.DeviceBuffer(self.local, arr.nbytes).upload(arr)
+        else:
+            b = self.torch.from_numpy(np.ascontiguousarray(arr).view(np.uint8).reshape(-1).copy()).to(
+                f"cuda:{self.local}")
+        self.keep.append(b)
+        return b
+
+    def download(self, buf, arr):
+        if self.torch is None:
+            return buf.download(arr)
+        arr.view(np.uint8).reshape(-1)[:] = buf[:arr.nbytes].cpu().numpy()
+        return arr
+
+
+def run_suite(G, clk, FL, probe, hbm, bf16, src):
+    """All dtype x shape rows of the suite on device 0, default tiles, cold L2."""
+    from mlpgemm import formats as F
+    from mlpgemm.data import Operands
+    names = G.tile_names()
+    rows = []
+    shared_w = {}
+    for sname, N, K, M, iters in SUITE:
+        ops = Operands(N, K, M, "seeded", 0)
+        # the thin and fat rows share K and M, hence the very same seeded W planes
+        for k, v in shared_w.items():
+            ops._cache[k] = v
+        wdec_cache = {}
+        for dtype in F.DTYPES:
+            dt = F.CODE[dtype]
+            ti = G.default_tile(dt, N, K, M)
+            tile = names[ti]
+            d = Dev(G, 0)
+            X, W = d.upload(ops.X(dtype)), d.upload(ops.W(dtype))
+            XS, WS = d.upload(ops.xscale(dtype)), d.upload(ops.wscale(dtype))
+            Y = d.zeros(N * M * 4)
+            wsb = G.workspace_size(dt, ti, N, K, M)
+            WSP = d.zeros(wsb) if wsb else None
+            G.run(0, dt, ti, X, W, Y, N, K, M, XS, WS, WSP, wsb)
+            G.sync(0)
+            host = d.download(Y, np.empty((N, M), np.int32 if dtype == "i8i8" else np.float32))
+            wkey = ops.w_name(dtype)
+            if wkey not in wdec_cache:
+                wdec_cache[wkey] = ops.w_cols(dtype, np.arange(M))
+            ok, rel = check_rows_of(ops, dtype, host, parity_rows(N), 0, M, wdec_cache[wkey])
+            with clk.window() as w:
+                ms = G.time(0, dt, ti, X, [W], Y, N, K, M, xscale=XS, wscales=[WS] if WS is not None else None,
+                            workspace=WSP, workspace_bytes=wsb, warmup=3, iters=iters, flush=FL,
+                            flush_bytes=FLUSH_BYTES)
+            med = statistics.median(ms)
+            flops = 2.0 * N * K * M
+            kind = F.TC_KIND[dtype]
+            if dtype in ("mxfp4/a8", "mxfp4/f8"):
+                kind_probe = "mxf8f6f4"
+            else:
+                kind_probe = kind
+            row = {"shape": sname, "dtype": dtype, "N": N, "K": K, "M": M, "tile": tile,
+                   "ms_median": med, "ms_mean": statistics.mean(ms), "iters": iters,
+                   "value": flops / (med / 1e3) / 1e12, "unit": unit_of(dtype),
+                   "parity_ok": ok, "max_rel": rel, "clocks": w.summary()}
+            if N <= 16:
+                gbs = F.algorithmic_bytes(dtype, N, K, M) / (med / 1e3) / 1e9
+                row.update({"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / hbm,
+                            "peak": hbm, "peak_source": f"{src} hbm_gbs"})
+            else:
+                peak = bf16 * KIND_RATIO[kind]
+                pp = probe.get(kind_probe)
+                row.update({"bound": "tensor", "kind": kind, "frac": row["value"] / peak, "peak": peak,
+                            "peak_source": f"{src} bf16 burst x {KIND_RATIO[kind]:g} (dense kind::{kind})",
+                            "probe_kind": kind_probe, "probe_peak": pp,
+                            "probe_frac": (row["value"] / pp) if pp else None})
+            rows.append(row)
+            del d
+        if sname == "fat":
+            shared_w = {k: v for k, v in ops._cache.items() if k.startswith("w")}
+    return rows
+
+
+def e2e_measure(G, dev, dt, ti, ops, dtype, W, WS, Y, WSP, wsb, N, K, width, a, d):
+    """Pinned host X in, GEMM of this rank's block, its Y block out, per step."""
+    import ctypes
+    xh = ops.X(dtype)
+    xs = ops.xscale(dtype)
+    L = G.lib()
+    hX, hY = L.gemm_host_alloc(xh.nbytes), L.gemm_host_alloc(N * width * 4)
+    hXS = L.gemm_host_alloc(xs.nbytes) if xs is not None else None
+    try:
+        ctypes.memmove(hX, xh.ctypes.data, xh.nbytes)
+        if xs is not None:
+            ctypes.memmove(hXS, xs.ctypes.data, xs.nbytes)
+        iters = max(5, min(a.steps, 30))
+        X1, X2 = d.empty(xh.nbytes), d.empty(xh.nbytes)
+        Y2 = d.empty(N * width * 4)
+        XS1 = d.empty(xs.nbytes) if xs is not None else None
+        XS2 = d.empty(xs.nbytes) if xs is not None else None
+        ms = G.time_e2e(dev, dt, ti, hX, X1, W, Y, hY, N, K, width, hXS, XS1, WS, WSP, wsb,
+                        warmup=max(3, a.warmup), iters=iters)
+        total = G.time_e2e_pipelined(dev, dt, ti, hX, (X1, X2), W, (Y, Y2), hY, N, K, width, hXS, (XS1, XS2), WS,
+                                     WSP, wsb, warmup=max(3, a.warmup), iters=iters)
+    finally:
+        L.gemm_host_free(hX)
+        L.gemm_host_free(hY)
+        if hXS:
+            L.gemm_host_free(hXS)
+    h2d = xh.nbytes + (xs.nbytes if xs is not None else 0)
+    return {"ms_per_step": total / iters, "serial_ms_per_step": statistics.mean(ms), "steps": iters,
+            "h2d": h2d, "d2h": N * width * 4}
 
 
 def ours(a):
     from mlpgemm import dist_util as DU
     from mlpgemm import formats as F
     from mlpgemm import lib as G
-    from mlpgemm.data import Operands
+    from mlpgemm.data import Operands, shard_columns
+    from mlpgemm.shard import shard_plan
 
     world, rank, local = dist_env()
-    dist = None
+    torch = dist = None
     if world > 1:
         import datetime
 
@@ -278,162 +497,207 @@ def ours(a):
     G.init(local)
     dtype, N, K, M = a.dtype, a.N, a.K, a.M
     dt = F.CODE[dtype]
-    tile = a.tile or G.tile_names()[G.default_tile(dt, N, K, M)]
+    names = G.tile_names()
+    plan = shard_plan(M, world)
+    m0, width = plan[rank]
+    tile = a.tile or names[G.default_tile(dt, N, K, width)]
     ti = G.tile_index(tile)
-    # weak scaling: rank r owns columns [r*M, (r+1)*M) of a world*M-wide GEMM;
-    # its W slice is generated with its own seed (independent column block)
-    ops = Operands(N, K, M, "seeded", seed=rank)
-    X = G.DeviceBuffer(local, ops.X(dtype).nbytes).upload(ops.X(dtype))
-    W = G.DeviceBuffer(local, ops.W(dtype).nbytes).upload(ops.W(dtype))
-    xs, ws = ops.xscale(dtype), ops.wscale(dtype)
-    XS = G.DeviceBuffer(local, xs.nbytes).upload(xs) if xs is not None else None
-    WS = G.DeviceBuffer(local, ws.nbytes).upload(ws) if ws is not None else None
-    Y = G.DeviceBuffer(local, N * M * 4).zero()
-    wsb = G.workspace_size(dt, ti, N, K, M)
-    WSP = G.DeviceBuffer(local, wsb).zero() if wsb else None
-    FL = G.DeviceBuffer(local, FLUSH_BYTES).zero()
+    d = Dev(G, local, torch)
+    ops = Operands(N, K, M, "seeded", 0)
+    hbm, bf16, src = peaks()
 
-    # parity gate on this rank's own output before timing (sample rows)
-    G.run(local, dt, ti, X, W, Y, N, K, M, XS, WS, WSP, wsb)
+    # X: replicated.  Under torchrun rank 0 uploads it and NCCL broadcasts it once.
+    xh = ops.X(dtype)
+    bcast_ms = None
+    if dist is None:
+        X = d.upload(xh)
+    else:
+        X = d.empty(xh.nbytes)
+        if rank == 0:
+            X.copy_(torch.from_numpy(xh.view(np.uint8).reshape(-1).copy()))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dist.broadcast(X, src=0)
+        e1.record()
+        torch.cuda.synchronize()
+        bcast_ms = e0.elapsed_time(e1)
+    XS = d.upload(ops.xscale(dtype))
+    # this rank's column block of W (and of its scale plane)
+    Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
+    assert w == width
+    W = d.upload(Wsh)
+    WS = d.upload(wsc)
+    Y = d.zeros(N * width * 4)
+    wsb = G.workspace_size(dt, ti, N, K, width)
+    WSP = d.zeros(wsb) if wsb else None
+    FL = d.zeros(FLUSH_BYTES)
+
+    # parity gate on this rank's own block before timing: whole rows, all its columns
+    G.run(local, dt, ti, X, W, Y, N, K, width, XS, WS, WSP, wsb)
     G.sync(local)
-    ok = check_rows(G, ops, dtype, Y, N, M)
+    host = d.download(Y, np.empty((N, width), np.int32 if dtype == "i8i8" else np.float32))
+    prow = parity_rows(N)
+    ok, rel = check_rows_of(ops, dtype, host, prow, m0, width)
 
     def barrier():
         if dist is not None:
             dist.barrier()
 
-    barrier()
-    with ClockSampler(local) as clk:
-        ms = G.time(local, dt, ti, X, [W], Y, N, K, M, xscale=XS, wscales=[WS] if WS else None,
-                    workspace=WSP, workspace_bytes=wsb, warmup=a.warmup, iters=a.steps,
-                    flush=FL, flush_bytes=FLUSH_BYTES)
-    barrier()
-    total_ms = float(sum(ms))
-    if dist is not None:
-        total_ms = DU.reduce_max(dist, total_ms, "cuda")
-        ok = DU.reduce_all(dist, ok, "cuda")
-    flops = 2.0 * N * K * M
-    value = DU.weak_scaling_rate(flops, world, a.steps, total_ms)
+    with ClockSampler(nvml_index(local)) as clk:
+        barrier()
+        with clk.window() as win:
+            ms = G.time(local, dt, ti, X, [W], Y, N, K, width, xscale=XS, wscales=[WS] if WS is not None else None,
+                        workspace=WSP, workspace_bytes=wsb, warmup=a.warmup, iters=a.steps,
+                        flush=FL, flush_bytes=FLUSH_BYTES)
+        barrier()
+        clocks = win.summary()
+        total_ms = float(sum(ms))
+        per_launch_ms = statistics.mean(ms)
+        if dist is not None:
+            total_ms = DU.reduce_max(dist, total_ms, "cuda")
+            ok = DU.reduce_all(dist, ok, "cuda")
+            rel = DU.reduce_max(dist, rel, "cuda")
+        flops = 2.0 * N * K * M
+        value = DU.strong_scaling_rate(flops * a.steps, total_ms)
 
-    # end to end through the C ABI: pinned host X in, device GEMM, host Y out,
-    # every rank at once (they share the host's memory); the job's rate is set
-    # by the slowest rank, as for `value`
-    if dist is not None:
-        dist.barrier()
-    e2e = e2e_measure(G, local, dtype, dt, ti, ops, X, W, XS, WS, Y, WSP, wsb, N, K, M, a)
-    if dist is not None:
-        t_max = DU.reduce_max(dist, e2e["ms_per_step"], "cuda")
-        t_ser = DU.reduce_max(dist, e2e["serial"]["ms_per_step"], "cuda")
-        dist.barrier()
-        dist.destroy_process_group()
-    else:
-        t_max, t_ser = e2e["ms_per_step"], e2e["serial"]["ms_per_step"]
-    flops_job = 2.0 * N * K * M * world
-    e2e.update({"value": flops_job / (t_max / 1e3) / 1e12, "ms_per_step": t_max,
-                "h2d_bytes_per_step": e2e["h2d_bytes_per_step"] * world,
-                "d2h_bytes_per_step": e2e["d2h_bytes_per_step"] * world, "ranks": world})
-    e2e["serial"].update({"value": flops_job / (t_ser / 1e3) / 1e12, "ms_per_step": t_ser})
-    if rank != 0:
-        return 0 if ok else 3
+        # end to end through the C ABI, every rank at once (they share the host)
+        barrier()
+        e = e2e_measure(G, local, dt, ti, ops, dtype, W, WS, Y, WSP, wsb, N, K, width, a, d)
+        t_pipe, t_ser = e["ms_per_step"], e["serial_ms_per_step"]
+        if dist is not None:
+            t_pipe = DU.reduce_max(dist, t_pipe, "cuda")
+            t_ser = DU.reduce_max(dist, t_ser, "cuda")
+        e2e = {"value": flops / (t_pipe / 1e3) / 1e12, "unit": unit_of(dtype),
+               "h2d_bytes_per_step": e["h2d"] * world, "d2h_bytes_per_step": N * M * 4,
+               "ms_per_step": t_pipe, "steps": e["steps"], "ranks": world,
+               "path": "gemm_time_e2e_pipelined on every rank: per step pinned host X -> device, gemm_run on the "
+                       "rank's column block, its Y block -> pinned host; consecutive steps overlapped two deep "
+                       "on three streams; the job's step is the slowest rank's",
+               "serial": {"value": flops / (t_ser / 1e3) / 1e12, "ms_per_step": t_ser,
+                          "path": "gemm_time_e2e: the same three steps back to back"}}
 
-    hbm, bf16, src = peaks()
-    kind = F.TC_KIND[dtype] if not tile.startswith("gemv") else "hbm"
-    per_launch_s = statistics.mean(ms) / 1e3
-    if kind == "hbm":
-        achieved = F.algorithmic_bytes(dtype, N, K, M) / per_launch_s / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)" if src == "measured" else "fallback 6650 GB/s"}
-    else:
-        peak = bf16 * KIND_RATIO[kind]
-        achieved = flops / per_launch_s / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak,
-                "unit": "TOPS" if dtype == "i8i8" else "TFLOP/s",
-                "peak_source": (f"{src}: bf16_tflops burst {bf16} x {KIND_RATIO[kind]:g} "
-                                f"(dense kind::{kind} : bf16 rate of B200)")}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    key = f"{dtype} {tile} N={N} K={K} M={M}"
-    roof["traffic"] = traffic_for(key)
-    roof["algorithmic_bytes"] = F.algorithmic_bytes(dtype, N, K, M)
-    roof["kernel_ms_mean"] = per_launch_s * 1e3
-    roof["kernel_ms_median"] = statistics.median(ms)
+        sharded = None
+        if dist is not None and not a.no_gathers:
+            sharded = gathers(a, torch, dist, world, rank, local, ops, dtype, N, K, M)
+            sharded.update({"bcast_ms": bcast_ms, "plan": [list(p) for p in plan]})
 
-    line = {
-        "metric": BASELINE_METRIC, "value": value, "unit": unit_of(dtype), "n_gpus": world,
-        "steps": a.steps, "warmup": a.warmup, "ms_per_step": total_ms / a.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int8" if dtype == "i8i8" else dtype, "data": "synthetic",
-        "config": {"workload": workload_name(dtype, N, K, M), "N": N, "K": K, "M": M,
-                   "tile": tile, "per_gpu": f"each rank computes its own [{N},{M}] column block "
-                                             f"of a [{N},{M * world}] output",
-                   "l2": "flushed: a 256 MiB buffer is read before every timed step, outside its events",
-                   "operands": "seeded i.i.d. int8 U{-127..127}" if dtype == "i8i8" else "seeded",
-                   "accumulate": "int32" if dtype == "i8i8" else "f32",
-                   "parity": "bit-exact vs int64 dot product" if dtype == "i8i8" else "rel<=1e-3 vs fp64",
-                   "parity_ok": ok},
-        "e2e": e2e,
-        "roofline": roof,
-        "gpu_launches": a.steps * G.launches_per_run(dt, ti, N, K, M),
-        "clocks": clk.summary(),
-    }
-    if not a.no_cpu_baseline and world == 1:
-        v, rows, thr, el = cpu_sample(dtype, N, K, M, seconds=10.0)
+        line = None
+        if rank == 0:
+            kind = F.TC_KIND[dtype]
+            achieved = 2.0 * N * K * width / (per_launch_ms / 1e3) / 1e12
+            if tile.startswith("gemv") or tile == "16x128" or tile == "stream":
+                gbs = F.algorithmic_bytes(dtype, N, K, width) / (per_launch_ms / 1e3) / 1e9
+                roof = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                        "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)"}
+            else:
+                peak = bf16 * KIND_RATIO[kind]
+                roof = {"bound": "tensor", "achieved": achieved, "peak": peak,
+                        "unit": "TOPS" if dtype == "i8i8" else "TFLOP/s",
+                        "peak_source": (f"{src}: bf16_tflops burst {bf16} x {KIND_RATIO[kind]:g} "
+                                        f"(dense kind::{kind} : bf16 rate of B200)")}
+            roof["frac"] = roof["achieved"] / roof["peak"]
+            tr = traffic_for(f"{dtype} {tile} N={N} K={K} M={width}")
+            roof["traffic"] = tr.get("dram_bytes_per_launch") if tr else None
+            if tr:
+                roof["traffic_note"] = tr.get("note", "")
+            roof["algorithmic_bytes"] = F.algorithmic_bytes(dtype, N, K, width)
+            roof["kernel_ms_mean"] = per_launch_ms
+            roof["kernel_ms_median"] = statistics.median(ms)
+            roof["kernel"] = f"{dtype} tile {tile} on rank 0's [{N},{width}] block"
+            line = {
+                "metric": BASELINE_METRIC, "value": value, "unit": unit_of(dtype), "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": total_ms / a.steps,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": {"i8i8": "int8", "f8f8": "e4m3"}.get(dtype, dtype), "data": "synthetic",
+                "config": workload_config(dtype, N, K, M, world),
+                "tile": tile,
+                "parity": {"ok": ok, "max_rel": rel, "rows": prow,
+                           "check": ("bit-exact vs an exact dot product" if dtype == "i8i8" else
+                                     "max rel <= 1e-3 vs an fp64 numpy dot product of the decoded operands, "
+                                     "denominator max(|ref|, 1e-2 rms)"),
+                           "scope": "whole rows of every rank's column block"},
+                "e2e": e2e, "roofline": roof,
+                "gpu_launches": a.steps * G.launches_per_run(dt, ti, N, K, width),
+                "clocks": clocks,
+            }
+            if sharded is not None:
+                line["sharded"] = sharded
+        # per-rank clocks of the timed region
+        if dist is not None:
+            rec = torch.tensor([clocks["sm_mhz"] or 0.0, clocks["sm_min_mhz"] or 0.0,
+                                float(sum(REASON_BITS[r] for r in clocks["reasons"])), float(clocks["samples"])],
+                               dtype=torch.float64, device=f"cuda:{local}")
+            allr = [torch.zeros_like(rec) for _ in range(world)]
+            dist.all_gather(allr, rec)
+            if rank == 0:
+                line["clocks"]["per_rank"] = [{"sm_mhz": r[0].item(), "sm_min_mhz": r[1].item(),
+                                               "reasons": sorted(k for k, v in REASON_BITS.items()
+                                                                 if int(r[2].item()) & v),
+                                               "samples": int(r[3].item())} for r in allr]
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank != 0:
+            return 0 if ok else 3
+
+        if world == 1:
+            probe = {}
+            for kname, kid in PROBE_KIND.items():
+                with clk.window():
+                    probe[kname] = G.peak_probe(local, kid, 4096, 5)
+            line["probe"] = {k: round(v, 1) for k, v in probe.items()}
+            line["probe"]["what"] = "gemm_peak_probe: tcgen05 MMAs on operands resident in shared memory, 1 CTA/SM"
+            if not a.no_suite:
+                del d, X, W, Y, WSP
+                suite = run_suite(G, clk, FL, probe, hbm, bf16, src)
+                line["suite"] = {"rows": suite, "n": len(suite), "parity_ok": all(r["parity_ok"] for r in suite),
+                                 "what": ("every dtype x shape of the reference's suite (main.swift:156-160), "
+                                          "default tile, L2 flushed before every timed launch, median of the "
+                                          "CUDA-event times; frac = of the measured per-kind peak (thin rows: "
+                                          "of the measured HBM copy bandwidth), probe_frac = of gemm_peak_probe"),
+                                 "clocks": clk.summary()}
+                ok = ok and line["suite"]["parity_ok"]
+    if world == 1 and not a.no_cpu_baseline:
+        v, rows, thr, el = cpu_sample(dtype, ops, seconds=10.0)
         line["cpu_baseline"] = {"value": v, "unit": unit_of(dtype), "cores": thr, "kind": "port",
-                                "sample": f"{rows} of {N} output rows (all {M} columns, K={K}) in "
-                                          f"{el:.1f} s: the reference's host dot product "
-                                          f"(main.swift:563-583) as an OpenMP host GEMM"}
+                                "sample": f"{rows} of {N} output rows (all {M} columns, K={K}) in {el:.1f} s: "
+                                          f"the reference's host dot product (main.swift:577-583) as an OpenMP "
+                                          f"host GEMM (oracle/mlp_oracle.c)"}
     print(json.dumps(line))
+    sys.stdout.flush()
     return 0 if ok else 3
 
 
-def check_rows(G, ops, dtype, Y, N, M, nrows=4):
-    host = np.empty((N, M), dtype=np.int32 if dtype == "i8i8" else np.float32)
-    Y.download(host)
-    rows = sorted({0, N - 1, N // 2, min(N - 1, 129)})[:nrows]
-    ref = ops.x_rows(dtype, rows) @ ops.w_cols(dtype, np.arange(M))
-    got = host[rows].astype(np.float64)
-    if dtype == "i8i8":
-        return bool(np.array_equal(got, ref))
-    rms = float(np.sqrt(np.mean(ref * ref)))
-    return bool(np.all(np.abs(got - ref) <= 1e-3 * np.maximum(np.abs(ref), 1e-2 * rms)))
-
-
-def e2e_measure(G, dev, dtype, dt, ti, ops, X, W, XS, WS, Y, WSP, wsb, N, K, M, a):
-    import ctypes
-    xh = ops.X(dtype)
-    hX = G.lib().gemm_host_alloc(xh.nbytes)
-    hY = G.lib().gemm_host_alloc(N * M * 4)
-    hXS = None
-    xs = ops.xscale(dtype)
-    try:
-        ctypes.memmove(hX, xh.ctypes.data, xh.nbytes)
-        if xs is not None:
-            hXS = G.lib().gemm_host_alloc(xs.nbytes)
-            ctypes.memmove(hXS, xs.ctypes.data, xs.nbytes)
-        iters = max(5, min(a.steps, 30))
-        # each step alone: copy in, GEMM, copy out back to back
-        ms = G.time_e2e(dev, dt, ti, hX, X, W, Y, hY, N, K, M, hXS, XS, WS, WSP, wsb,
-                        warmup=max(3, a.warmup), iters=iters)
-        # the serving loop: consecutive steps overlapped two deep (second X / Y set)
-        X2 = G.DeviceBuffer(dev, xh.nbytes)
-        Y2 = G.DeviceBuffer(dev, N * M * 4)
-        XS2 = G.DeviceBuffer(dev, xs.nbytes) if xs is not None else None
-        total = G.time_e2e_pipelined(dev, dt, ti, hX, (X, X2), W, (Y, Y2), hY, N, K, M, hXS, (XS, XS2), WS,
-                                     WSP, wsb, warmup=max(3, a.warmup), iters=iters)
-    finally:
-        G.lib().gemm_host_free(hX)
-        G.lib().gemm_host_free(hY)
-        if hXS:
-            G.lib().gemm_host_free(hXS)
-    t_serial = statistics.mean(ms) / 1e3
-    t = total / iters / 1e3
-    h2d = xh.nbytes + (xs.nbytes if xs is not None else 0)
-    return {"value": 2.0 * N * K * M / t / 1e12, "unit": unit_of(dtype),
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": N * M * 4,
-            "ms_per_step": t * 1e3, "steps": iters,
-            "path": "gemm_time_e2e_pipelined: per step pinned host X -> device, gemm_run, device Y -> "
-                    "pinned host, consecutive steps overlapped two deep on three streams",
-            "serial": {"value": 2.0 * N * K * M / t_serial / 1e12, "ms_per_step": t_serial * 1e3,
-                       "path": "gemm_time_e2e: the same three steps back to back"}}
+def gathers(a, torch, dist, world, rank, local, ops, dtype, N, K, M):
+    """The collectives beside the sharded GEMM, each timed separately (median
+    of 5 after a warm-up, max over ranks): the M-sharded Y all-gathered by
+    NCCL and permuted to [N, M]; the N-sharded GEMM with its NCCL all-gather
+    in place; the fused GEMM + all-gather over NVLink peer stores.  Every
+    rank's gathered Y is checked against numpy rows (check_samples) and the
+    fused Y against the NCCL-gathered Y bit for bit (mlpgemm.shard)."""
+    from mlpgemm import shard
+    from mlpgemm.driver import Args, ShapeCase
+    sa = Args()
+    sa.dtypes = [dtype]
+    sa.allgather = True
+    sa.data, sa.seed = "seeded", 0
+    sa.warmup = 2
+    sa.tile = a.tile
+    sa.use_profile = False
+    sa.gpus = world
+    shape = ShapeCase(shape_name(N, K, M), N, K, M, 10)
+    _, em = shard.run_shape(sa, shape, torch, dist, world, rank, local, {}, ops=ops)
+    _, en = shard.run_shape_rows(sa, shape, torch, dist, world, rank, local, {}, ops=ops)
+    _, _, _, _, ag, mblk, mgemm, mpipe, _ = em[0]
+    _, _, _, _, nag, nblk, ngemm, npipe, fused = en[0]
+    return {"mshard_gemm_ms": mgemm, "allgather_ms": ag, "mshard_pipeline_ms": mpipe,
+            "nshard_block": nblk, "nshard_gemm_ms": ngemm, "nshard_gather_ms": nag,
+            "nshard_pipeline_ms": npipe, "fused_ms": fused, "fused_equals_nccl": fused is not None,
+            "what": ("allgather_ms: NCCL all-gather of the M-sharded Y blocks + permute to [N,M]; "
+                     "nshard_gather_ms: rows of X per GPU, W replicated, NCCL all-gather in place into Y; "
+                     "fused_ms: gemm_run_gather (N-sharded GEMM whose epilogue stores each Y tile into every "
+                     "GPU's Y over NVLink) + a 1-element all-reduce; *_pipeline_ms: GEMM chunks overlapped "
+                     "with NCCL all-gathers on a second stream. Medians over 5 runs, max over ranks.")}
 
 
 def main():

@@ -1457,6 +1457,15 @@ int current_device() {
   return d;
 }
 
+// One-time set-up of a kernel per device (the dynamic shared-memory opt-in and,
+// for the pair kernel, its co-resident cluster count).  The lock keeps host
+// threads that launch on the same device at the same time from racing on it.
+struct DevOnce {
+  std::mutex mu;
+  unsigned mask = 0;      // bit d: device d is set up
+  int value[32] = {0};    // per-device result (max co-resident CTA pairs)
+};
+
 template <int DT, int BN, int STAGES>
 cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nullptr,
                        const uint8_t* sfb = nullptr) {
@@ -1504,12 +1513,15 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   p.split_from = p.num_items = tiles;   // whole tiles only
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_gemm_kernel<DT, BN, STAGES>;
-  static unsigned attr_mask = 0;   // per device: dynamic shared memory opt-in done
+  static DevOnce once;   // per device: dynamic shared memory opt-in done
   const int dev = current_device();
-  if (!(attr_mask & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_mask |= 1u << (dev & 31);
+  {
+    std::lock_guard<std::mutex> lk(once.mu);
+    if (!(once.mask & (1u << (dev & 31)))) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      once.mask |= 1u << (dev & 31);
+    }
   }
   k<<<grid, kThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmB, p);
   return cudaGetLastError();
@@ -1576,8 +1588,7 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   set_peers(p, a);
   const int tiles = p.tiles_m * p.tiles_n;
   auto k = tc_gemm_pair_kernel<DT, BN, STAGES>;
-  static unsigned attr_mask = 0;
-  static int max_pairs[32] = {0};   // co-resident CTA pairs per device (persistent grid size)
+  static DevOnce once;   // per device: shared-memory opt-in and co-resident CTA pairs (grid size)
   const int dev = current_device();
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kThreads);
@@ -1590,16 +1601,21 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!(attr_mask & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    int n = 0;
-    cfg.gridDim = dim3(a.num_sms);
-    if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) n = a.num_sms / 2;
-    max_pairs[dev & 31] = n;
-    attr_mask |= 1u << (dev & 31);
+  int cap = 0;
+  {
+    std::lock_guard<std::mutex> lk(once.mu);
+    if (!(once.mask & (1u << (dev & 31)))) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      int n = 0;
+      cfg.gridDim = dim3(a.num_sms);
+      if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess || n <= 0) n = a.num_sms / 2;
+      once.value[dev & 31] = n;
+      once.mask |= 1u << (dev & 31);
+    }
+    cap = once.value[dev & 31];
   }
-  const int cap = max_pairs[dev & 31] > 0 ? max_pairs[dev & 31] : a.num_sms / 2;
+  if (cap <= 0) cap = a.num_sms / 2;
   const int pairs = tiles < cap ? tiles : cap;
   // a last wave of at most half the pairs runs as twice as many half tiles
   const int rem = tiles % pairs;
@@ -1657,12 +1673,15 @@ cudaError_t launch_widen(const RunArgs& a) {
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_widen_kernel<DT, BN, STAGES>;
-  static unsigned attr_mask = 0;
+  static DevOnce once;
   const int dev = current_device();
-  if (!(attr_mask & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_mask |= 1u << (dev & 31);
+  {
+    std::lock_guard<std::mutex> lk(once.mu);
+    if (!(once.mask & (1u << (dev & 31)))) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      once.mask |= 1u << (dev & 31);
+    }
   }
   k<<<grid, kWThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmR, p);
   return cudaGetLastError();

@@ -1050,9 +1050,15 @@ static int eff_splits(int K, int ksplit) {
 }
 
 bool gemv_supported(int dt, int ksplit, int N, int K, int M) {
-  (void)M;
   if (N < 1 || K < 1 || M < 1) return false;
-  return gemv_smem(dt, N, kchunk_for(K, ksplit < 1 ? 1 : ksplit)) <= kMaxGemvSmem;
+  if (gemv_smem(dt, N, kchunk_for(K, ksplit < 1 ? 1 : ksplit)) > kMaxGemvSmem) return false;
+  // splits above the cluster size meet through one workspace counter per output tile
+  if (eff_splits(K, ksplit) > kMaxClusterSplit) {
+    const int nr = pick_nr(N);
+    const long tiles = (long)((M + cols_per_cta(dt, N) - 1) / cols_per_cta(dt, N)) * ((N + nr - 1) / nr);
+    if (tiles > kMaxCounterTiles) return false;
+  }
+  return true;
 }
 
 int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {

@@ -83,12 +83,30 @@ extern "C" int gemm_run_noalloc(int device, int dtype, int ksplit, const void* X
   if (!X || !W || !Y) return err(GEMM_ERR_ARGS, "null operand");
   if (x_scaled(dtype) && !xscale) return err(GEMM_ERR_ARGS, "missing X scale plane");
   if (w_is_mx(dtype) && !wscale) return err(GEMM_ERR_ARGS, "missing W scale plane");
+  // the caller's current device is put back on every return path
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  struct Restore {
+    int dev;
+    ~Restore() {
+      if (dev >= 0) cudaSetDevice(dev);
+    }
+  } restore{prev};
   int rc;
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return err(GEMM_ERR_CUDA, cudaGetErrorString(e));
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (ksplit <= 0) ksplit = gemv_auto_ksplit(dtype, N, K, M, sms);
+  if (!gemv_supported(dtype, ksplit, N, K, M)) {
+    char m[256];
+    snprintf(m, sizeof m,
+             "ksplit=%d is not available for this dtype and shape (N=%d, K=%d, M=%d):"
+             " a split must fit the kernel's shared-memory budget, and above 8 splits the output's"
+             " tile count must fit the split-K counter region",
+             ksplit, N, K, M);
+    return err(GEMM_ERR_ARGS, m);
+  }
   const size_t need = gemv_workspace(dtype, ksplit, N, K, M);
   if (need > kNoAllocBytes) {
     char m[256];

@@ -39,6 +39,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <mutex>
 #include <type_traits>
 
 #include "formats.cuh"
@@ -593,13 +594,19 @@ cudaError_t launch_thin_dt(const RunArgs& a, int grid_cap = 0) {
   if (grid > kMaxThinCtas) grid = kMaxThinCtas;
   if (grid > p.units) grid = p.units;   // every CTA owns at least one unit
   auto k = tc_thin_kernel<DT, STAGES>;
-  static unsigned attr_mask = 0;   // per device: dynamic shared memory opt-in done
+  // per device: dynamic shared memory opt-in done (locked: host threads may
+  // launch on one device at the same time)
+  static std::mutex mu;
+  static unsigned attr_mask = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_mask & (1u << (dev & 31)))) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_mask |= 1u << (dev & 31);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(attr_mask & (1u << (dev & 31)))) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      attr_mask |= 1u << (dev & 31);
+    }
   }
   k<<<grid, C::THREADS, C::SMEM_BYTES, a.stream>>>(tmW, tmX, p);
   return cudaGetLastError();

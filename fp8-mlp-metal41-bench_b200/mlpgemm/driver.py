@@ -378,9 +378,12 @@ def bench_shape(a: Args, shape: ShapeCase, rn: Runner, profile: dict, out=print)
         if a.autotune:
             tune_iters = max(5, min(20, shape.iters // 5))
             results = []
+            # every candidate is timed with a cold L2 (a >L2 buffer read before each
+            # launch): a tile chosen on L2-resident weights would be the wrong one for
+            # weights that stream from HBM, which is the thin row's whole cost
             for cand in candidate_tiles(dtype, N, K, M):
                 ms, _ = run_dtype(rn, dtype, cand, N, K, M, 2, tune_iters, rotate=a.rotate,
-                                  flush=a.flush)
+                                  flush=True)
                 results.append((cand, sorted(ms)[len(ms) // 2]))
             results.sort(key=lambda r: r[1])
             tile = results[0][0]

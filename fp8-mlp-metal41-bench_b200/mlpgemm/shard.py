@@ -136,7 +136,10 @@ def _x_bytes_tensor(torch, ops: Operands, dtype: str, device):
     return torch.from_numpy(x.view(np.uint8).copy()).to(device)
 
 
-def run_shape(a, shape, torch, dist, world, rank, local, profile):
+def run_shape(a, shape, torch, dist, world, rank, local, profile, ops=None):
+    """The M-sharded GEMM of one shape for every dtype of `a` (`ops`: operands
+    to reuse, e.g. a caller's for a single dtype; generated from a.data/a.seed
+    when None)."""
     N, K, M = shape.N, shape.K, shape.M
     flops = 2.0 * N * K * M
     rows = []
@@ -150,7 +153,7 @@ def run_shape(a, shape, torch, dist, world, rank, local, profile):
         if not F.layout_ok(dtype, N, K, M):
             raise BenchExit(1, f"{dtype} needs even X/W counts and K a multiple of 32 "
                                f"(128 for FP8 × MXFP4)")
-        ops = Operands(N, K, M, a.data, a.seed)
+        ops = ops if ops is not None else Operands(N, K, M, a.data, a.seed)
         dt = F.CODE[dtype]
         tile = choose_tile(a, profile, dtype, N, K, width) if width > 0 else "gemv.k1"
         ti = G.tile_index(tile)
@@ -324,7 +327,7 @@ def _rank_rows(arr, row_bytes: int, blocks, ch: int):
     return out
 
 
-def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
+def run_shape_rows(a, shape, torch, dist, world, rank, local, profile, ops=None):
     """The N-sharded GEMM: rows of X split block-cyclically (row_blocks), W
     replicated. Each rank derives its X rows from the seeded generator; W is
     generated on rank 0 and broadcast once over NCCL (`bcast_ms`). The
@@ -341,7 +344,7 @@ def run_shape_rows(a, shape, torch, dist, world, rank, local, profile):
                                f"(128 for FP8 × MXFP4)")
         if dtype in F.X_FP4 and K % 2:
             raise BenchExit(1, f"row sharding of packed 4-bit {dtype} X needs an even K")
-        ops = Operands(N, K, M, a.data, a.seed)
+        ops = ops if ops is not None else Operands(N, K, M, a.data, a.seed)
         dt = F.CODE[dtype]
         ch, rounds, blocks = row_blocks(N, world, 1)
         r0, h = blocks[rank][0]
@@ -468,6 +471,10 @@ def _fused_rows(torch, dist, world, rank, local, dt, ti, Xr, Wt, XS, WS, WSP, ws
     reps of the max over ranks of that time (ms), after checking that the
     Y it leaves on this GPU equals the NCCL-gathered `Yref` bit for bit."""
     M = Yref.shape[1]
+    # one block per rank: this rank's rows sit at rank*ch, contiguous, in every
+    # GPU's Y; a multi-round plan would interleave blocks and is not supported
+    if rounds != 1 or h > ch:
+        raise ValueError(f"fused all-gather needs one row block per rank (rounds={rounds}, h={h}, ch={ch})")
     dev = torch.device("cuda", local)
     es = Yref.element_size()
     peer = PeerY(torch, dist, world, rank, local, rounds * world * ch * M * es)
@@ -484,14 +491,25 @@ def _fused_rows(torch, dist, world, rank, local, dt, ti, Xr, Wt, XS, WS, WSP, ws
         for _ in range(reps + 1):
             s.wait_stream(torch.cuda.current_stream(dev))
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # every rank starts the rep together, so launch skew stays out of the time
+            dist.barrier()
+            err = None
             with torch.cuda.stream(s):
+                flag.zero_()
                 e0.record(s)
                 if h > 0:
-                    G.run_gather(local, dt, ti, Xr, Wt, peer.own + off, h, K, M, xscale=XS, wscale=WS,
-                                 workspace=WSP, workspace_bytes=wsb, peers=others, stream=s.cuda_stream)
+                    try:
+                        G.run_gather(local, dt, ti, Xr, Wt, peer.own + off, h, K, M, xscale=XS, wscale=WS,
+                                     workspace=WSP, workspace_bytes=wsb, peers=others, stream=s.cuda_stream)
+                    except G.GemmError as ex:   # still take part in the all-reduce below
+                        err = ex
+                        flag.fill_(1.0)
+                # orders every rank after the peers' writes, and carries any rank's failure
                 dist.all_reduce(flag)
                 e1.record(s)
             torch.cuda.synchronize(dev)
+            if float(flag.item()) != 0.0:   # the same decision on every rank
+                raise BenchExit(4, f"fused all-gather failed on a rank: {err or 'see that rank'}")
             times.append(e0.elapsed_time(e1))
         N = Yref.shape[0]
         same = bool(torch.equal(Yf[:N], Yref))

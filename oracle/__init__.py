@@ -260,11 +260,18 @@ def host_gemm_i32(X: np.ndarray, W: np.ndarray, K: int, M: int, row0: int,
 
 
 def full_reference(dtype, X, W, xscale, wscale, N, K, M):
-    """fp64 (or exact int64 for i8i8) Y over the whole output, for small shapes."""
+    """fp64 Y over the whole output (exact int64 for i8i8).
+
+    i8i8 (main.swift:563-568): the product runs as an fp64 BLAS GEMM and is
+    exact, whatever order the BLAS sums in: every product is an integer of
+    magnitude <= 127*127 < 2^14, so every partial sum is an integer below
+    K * 2^14 < 2^53 for any K < 2^39, and fp64 represents all of them.  (A
+    numpy int64 matmul gives the same values without BLAS, far too slowly for
+    the 4096^3 suite shape.)"""
     if code(dtype) == CODE["i8i8"]:
-        x = np.asarray(X, np.int8).reshape(N, K).astype(np.int64)
-        w = np.asarray(W, np.int8).reshape(K, M).astype(np.int64)
-        return x @ w
+        x = np.asarray(X, np.int8).reshape(N, K).astype(np.float64)
+        w = np.asarray(W, np.int8).reshape(K, M).astype(np.float64)
+        return (x @ w).astype(np.int64)
     xd = decode_x(dtype, X, xscale, N, K)
     wd = decode_w(dtype, W, wscale, K, M)
     return xd @ wd

@@ -407,10 +407,12 @@ int orc_sample_points(long N, long M, int bm, int bn, long *rows, long *cols)
 #define ORC_RB 4     /* output rows per task (share the W stream) */
 #define ORC_CB 256   /* output columns per task */
 
+/* every processor this process may run on, whatever OMP_NUM_THREADS says
+   (launchers such as torchrun set it to 1 per rank) */
 int orc_num_threads(void)
 {
 #ifdef _OPENMP
-    return omp_get_max_threads();
+    return omp_get_num_procs();
 #else
     return 1;
 #endif
@@ -422,7 +424,7 @@ void orc_host_gemm_f32(const float *xf, const float *wf, long K, long M,
     long rblocks = (nrows + ORC_RB - 1) / ORC_RB;
     long cblocks = (M + ORC_CB - 1) / ORC_CB;
 #ifdef _OPENMP
-    if (nthreads <= 0) nthreads = omp_get_max_threads();
+    if (nthreads <= 0) nthreads = omp_get_num_procs();
 #pragma omp parallel for collapse(2) schedule(dynamic, 1) num_threads(nthreads)
 #endif
     for (long rb = 0; rb < rblocks; ++rb) {
@@ -453,7 +455,7 @@ void orc_host_gemm_i32(const int8_t *X, const int8_t *W, long K, long M,
     long rblocks = (nrows + ORC_RB - 1) / ORC_RB;
     long cblocks = (M + ORC_CB - 1) / ORC_CB;
 #ifdef _OPENMP
-    if (nthreads <= 0) nthreads = omp_get_max_threads();
+    if (nthreads <= 0) nthreads = omp_get_num_procs();
 #pragma omp parallel for collapse(2) schedule(dynamic, 1) num_threads(nthreads)
 #endif
     for (long rb = 0; rb < rblocks; ++rb) {

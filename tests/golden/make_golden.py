@@ -20,7 +20,7 @@ as TEXT (it executes nothing from the reference) and writes them as JSON:
     log_lines          the header / autotune / running lines of the log
     profiles           the two published profile JSON files, verbatim
 
-Run:  python tests/golden/make_golden.py [/path/to/reference]
+Run:  python tests/golden/make_golden.py /path/to/reference
 The committed JSON is what the tests read; the reference tree is not needed
 at test time.
 """
@@ -116,7 +116,9 @@ def outputs(ref):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path to the reference checkout>")
+    ref = sys.argv[1]
     for name, obj in (("reference_tables.json", tables(ref)),
                       ("reference_outputs.json", outputs(ref))):
         path = os.path.join(HERE, name)

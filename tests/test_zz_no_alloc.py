@@ -6,11 +6,16 @@ allocator): it keeps the split-K scratch of the thin-row kernel in a fixed
 device array inside the library instead of a caller workspace.  It must give
 the same result as gemm_run with the matching "gemv.k<S>" tile and a
 workspace, on two calls in a row (the array keeps the previous call's
-contents).  This file is named so that pytest collects it last; it also runs
-alone in a fresh process (its only fixture initialises device 0)."""
+contents).  Both entry points run the same kernel with the same split and
+the same fixed reduction order, so the results must be identical bit for
+bit; the output is also checked against the oracle (bit-exact for i8i8,
+max relative error <= 1e-3 against fp64 for the float dtypes).  This file is
+named so that pytest collects it last; it also runs alone in a fresh process
+(its only fixture initialises device 0)."""
 import numpy as np
 import pytest
 
+import oracle
 from mlpgemm import formats as F
 from mlpgemm.data import Operands
 
@@ -44,18 +49,21 @@ def test_noalloc_matches_gemm_run_twice(gemm, dtype, N, K, M, ksplit):
     G.sync(0)
     want = Y0.download(np.empty((N, M), host_t))
 
+    ref = oracle.full_reference(dtype, ops.X(dtype), ops.W(dtype), ops.xscale(dtype), ops.wscale(dtype),
+                                N, K, M)
     for call in range(2):
         Y = G.DeviceBuffer(0, N * M * 4).zero()
         G.run_noalloc(0, dt, ksplit, X, W, Y, N, K, M, XS, WS)
         G.sync(0)
         got = Y.download(np.empty((N, M), host_t))
+        # same kernel, same split, same reduction order: the same bits
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"call {call}"
         if dtype == "i8i8":
-            assert np.array_equal(got, want), f"call {call}"
+            assert np.array_equal(got.astype(np.int64), ref), f"call {call}"
         else:
-            # same kernel, same reduction order: equal within the parity tolerance
-            rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
-            rel = np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1e-2 * rms)
-            assert rel.max() <= 1e-3, f"call {call}: max rel {rel.max():.3g}"
+            rms = float(np.sqrt(np.mean(ref * ref)))
+            rel = np.abs(got.astype(np.float64) - ref) / np.maximum(np.abs(ref), 1e-2 * rms)
+            assert rel.max() <= 1e-3, f"call {call}: max rel {rel.max():.3g} against the oracle"
 
 
 def test_noalloc_rejects_oversized_scratch(gemm):
@@ -65,3 +73,14 @@ def test_noalloc_rejects_oversized_scratch(gemm):
         G.run_noalloc(0, F.CODE["fp8"], 64, 1, 1, 1, 16, 4096, 11008)
     assert e.value.code == G.GEMM_ERR_ARGS
     assert "exceeds" in G.last_error()
+
+
+def test_noalloc_rejects_a_split_the_kernel_cannot_take(gemm):
+    G = gemm
+    # 64 splits of N = 16 rows by M = 2^20 columns need more split-K counter
+    # tiles than the counter region holds: rejected with a reason before any
+    # launch (the operand pointers are never used)
+    with pytest.raises(G.GemmError) as e:
+        G.run_noalloc(0, F.CODE["fp16"], 64, 1, 1, 1, 16, 4096, 1 << 20)
+    assert e.value.code == G.GEMM_ERR_ARGS
+    assert "ksplit" in G.last_error()
