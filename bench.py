@@ -63,9 +63,10 @@ import numpy as np  # noqa: E402
 FLUSH_BYTES = 256 << 20
 BASELINE_METRIC = "TFLOPS/TOPS per dtype×shape at 1/2/4/8 B200; % of tensor-peak or HBM roofline"
 # the reference's suite shapes (main.swift:156-160); iterations per suite row
-SUITE = [("square", 4096, 4096, 4096, 20), ("fat", 2048, 4096, 11008, 20), ("thin", 1, 4096, 11008, 50)]
+SUITE = [("square", 4096, 4096, 4096, 50), ("fat", 2048, 4096, 11008, 50), ("thin", 1, 4096, 11008, 100)]
 KIND_RATIO = {"f16": 1.0, "i8": 2.0, "f8f6f4": 2.0, "mxf4": 4.0}
-PROBE_KIND = {"f16": 0, "i8": 1, "f8f6f4": 2, "mxf8f6f4": 3, "mxf4": 4}
+PROBE_KIND = {"f16": 0, "i8": 1, "f8f6f4": 2, "mxf8f6f4": 3, "mxf4": 4,
+              "f16_pair_bmn": 8, "i8_pair_bmn": 9, "f8f6f4_pair_bmn": 10}
 
 
 def parse():

@@ -129,6 +129,9 @@ struct TcParams {
   int* dev_err;
   uint32_t* peer[kMaxPeers];   // peer Y bases: every Y store is repeated at the same offset
   int npeers;
+  // 1: the epilogue stores Y (and the peers' Y) through the TMA with the maps
+  // of EpiMaps (rows of M % 4 == 0 words, Y 16-byte aligned); 0: plain stores
+  int y_tma;
   // CTA-pair kernel work items: tiles 0 .. split_from-1 whole, then every
   // later tile as two 256 x BN/2 halves (the last, partial wave spread over
   // twice the pairs); split_from = num_items = the tile count when unsplit
@@ -191,6 +194,12 @@ struct Cfg {
   static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + STAGES * SF_COLS_STAGE);
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
+  // TMA-store epilogue: 4 KB staging buffers per epilogue warp, two where the
+  // shared-memory budget allows (a chunk's store overlaps the next chunk's
+  // staging), else one
+  static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
+  static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448 ? 2 : 1;
+  static constexpr int SMEM_EPI = EPI_OFF + 4 * EPI_BUFS * 4096 + 1024;
   static constexpr uint32_t IDESC =
       SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
                 ((uint32_t)(kBM >> 4) << 24))
@@ -200,12 +209,14 @@ struct Cfg {
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
   static_assert(!T::b_mn || BN % B_BOX_MN == 0, "MN-major B tile must be whole swizzle atoms");
   static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
-  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+  static_assert(SMEM_EPI <= 232448, "shared memory budget");
 };
 
-// Tensor maps of the peers' Y blocks (fused all-gather on CTA pairs): [N, M]
-// of 32-bit words from the peer's base pointer, 32 x 32 boxes, 128-byte swizzle.
-struct PeerMaps {
+// Tensor maps of the epilogue's TMA stores: this GPU's Y and the peers' Y
+// blocks (fused all-gather), each [N, M] of 32-bit words from its base
+// pointer, 32 x 32 boxes, 128-byte swizzle.
+struct EpiMaps {
+  CUtensorMap y;
   CUtensorMap m[kMaxPeers];
 };
 
@@ -360,7 +371,7 @@ __device__ __forceinline__ void store_peers(uint32_t (&r)[32], const TcParams& p
 // swizzle, which keeps the 32 row writes free of bank conflicts, and lane 0
 // stores the 32 x 32 box to every peer's map at (cb, row0).  The next chunk
 // waits until the TMA has read the buffer.
-__device__ __forceinline__ void store_peers_tma(const uint32_t (&r)[32], unsigned char* epi, const PeerMaps* pm,
+__device__ __forceinline__ void store_peers_tma(const uint32_t (&r)[32], unsigned char* epi, const EpiMaps* pm,
                                                 int npeers, int row0, int cb, int N, int M) {
   const int lane = (int)(threadIdx.x & 31u);
   const uint32_t base = smem_u32(epi);
@@ -383,39 +394,43 @@ __device__ __forceinline__ void store_peers_tma(const uint32_t (&r)[32], unsigne
   __syncwarp();
 }
 
+// f32 results of one 32-column chunk times 2^e per column (exact powers of
+// two; the A16 mxfp4 path's per-column exponent offsets).  The chunk's 32
+// exponents come in two 16-byte loads (the same for every lane); nothing is
+// done when all are zero, the usual case.
+__device__ __forceinline__ void apply_col_exp(uint32_t (&r)[32], const int8_t* col_exp, int cb, int M) {
+  uint32_t e4[8];
+  if (cb + 32 <= M) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(col_exp + cb));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(col_exp + cb + 16));
+    e4[0] = a.x, e4[1] = a.y, e4[2] = a.z, e4[3] = a.w, e4[4] = b.x, e4[5] = b.y, e4[6] = b.z, e4[7] = b.w;
+  } else {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      uint32_t x = 0;
+      for (int i = 0; i < 4; ++i)
+        if (cb + 4 * w + i < M) x |= (uint32_t)(uint8_t)col_exp[cb + 4 * w + i] << (8 * i);
+      e4[w] = x;
+    }
+  }
+  if ((e4[0] | e4[1] | e4[2] | e4[3] | e4[4] | e4[5] | e4[6] | e4[7]) != 0u) {
+#pragma unroll
+    for (int v = 0; v < 32; ++v) {
+      const int e = (int)(int8_t)(e4[v >> 2] >> (8 * (v & 3)));
+      if (e) r[v] = __float_as_uint(__uint_as_float(r[v]) * __int_as_float((e + 127) << 23));
+    }
+  }
+}
+
 template <int NCH, typename Release>
 __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, int col0, int M, bool row_ok,
                                                const int8_t* col_exp, const TcParams& p, int row0,
                                                Release release, unsigned char* epi = nullptr,
-                                               const PeerMaps* pm = nullptr) {
+                                               const EpiMaps* pm = nullptr) {
   const bool vec_ok = (M % 4) == 0;
   // this lane's row: column exponents (if any), then the local store
   auto store_row = [&](uint32_t (&r)[32], int cb) {
-    if (col_exp) {   // f32 results times 2^e per column (exact powers of two)
-      // the chunk's 32 exponents in two 16-byte loads (the same for every lane);
-      // nothing to do when all are zero, the usual case
-      uint32_t e4[8];
-      if (cb + 32 <= M) {
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(col_exp + cb));
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(col_exp + cb + 16));
-        e4[0] = a.x, e4[1] = a.y, e4[2] = a.z, e4[3] = a.w, e4[4] = b.x, e4[5] = b.y, e4[6] = b.z, e4[7] = b.w;
-      } else {
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          uint32_t x = 0;
-          for (int i = 0; i < 4; ++i)
-            if (cb + 4 * w + i < M) x |= (uint32_t)(uint8_t)col_exp[cb + 4 * w + i] << (8 * i);
-          e4[w] = x;
-        }
-      }
-      if ((e4[0] | e4[1] | e4[2] | e4[3] | e4[4] | e4[5] | e4[6] | e4[7]) != 0u) {
-#pragma unroll
-        for (int v = 0; v < 32; ++v) {
-          const int e = (int)(int8_t)(e4[v >> 2] >> (8 * (v & 3)));
-          if (e) r[v] = __float_as_uint(__uint_as_float(r[v]) * __int_as_float((e + 127) << 23));
-        }
-      }
-    }
+    if (col_exp) apply_col_exp(r, col_exp, cb, M);
     store_chunk(yrow, r, cb, M, vec_ok);
   };
   auto store = [&](uint32_t (&r)[32], int c) {
@@ -444,10 +459,69 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
   }
 }
 
+// Epilogue of one 32-row TMEM lane quadrant through the TMA (whole warp).
+// Each 32 x 32 chunk goes TMEM -> registers (tcgen05.ld), gets its column
+// exponents (if any), and is written into one of this warp's NBUF 4 KB
+// staging buffers (`epi`, 1024-byte aligned) with the 128-byte swizzle, so
+// the 32 row writes are free of bank conflicts; lane 0 then stores the
+// 32 x 32 box to this GPU's Y and to every peer's Y with one
+// cp.async.bulk.tensor each (rows past N and columns past M are clipped by
+// the TMA).  Compared with one 16-byte store per lane into 32 different rows,
+// the TMA writes whole 128-byte lines and leaves the SM's load/store path to
+// the operand stream.  `nst` counts this warp's stored chunks across tiles:
+// buffer nst % NBUF is rewritten only after the TMA has read it, i.e. once at
+// most NBUF - 1 newer store groups are pending.  Chunks with nothing to store
+// (past M, or a quadrant past N) write no buffer and commit no group; stored
+// chunks are a prefix of the tile's chunks.  `release` frees the accumulator
+// once the last chunk is in registers.
+template <int NCH, int NBUF, typename Release>
+__device__ __forceinline__ void drain_quadrant_tma(uint32_t taddr0, int col0, int row0, const TcParams& p,
+                                                   Release release, unsigned char* epi, const EpiMaps* em,
+                                                   int& nst) {
+  static_assert(NBUF >= 1 && NBUF <= 2, "one or two staging buffers");
+  static_assert(NCH % 2 == 0, "chunks come in pairs");
+  const int lane = (int)(threadIdx.x & 31u);
+  auto put = [&](uint32_t (&r)[32], int c) {
+    const int cb = col0 + c * 32;
+    if (row0 >= p.N || cb >= p.M) return;
+    if (p.col_exp) apply_col_exp(r, p.col_exp, cb, p.M);
+    const uint32_t base = smem_u32(epi) + (uint32_t)((nst % NBUF) * 4096);
+    if (lane == 0) bulk_wait_read<NBUF - 1>();   // the buffer's previous store has read it
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const uint32_t a = base + (uint32_t)lane * 128u + (uint32_t)((v ^ (lane & 7)) << 4);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(r[4 * v]), "r"(r[4 * v + 1]),
+                   "r"(r[4 * v + 2]), "r"(r[4 * v + 3])
+                   : "memory");
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(&em->y, base, cb, row0);
+      for (int i = 0; i < p.npeers; ++i) tma_store_2d(&em->m[i], base, cb, row0);
+      bulk_commit_group();
+    }
+    ++nst;
+  };
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(taddr0, ra);
+#pragma unroll 1
+  for (int c = 0; c < NCH; c += 2) {
+    tmem_ld_wait();                                            // chunk c in ra
+    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 1) * 32), rb);
+    put(ra, c);
+    tmem_ld_wait();                                            // chunk c + 1 in rb
+    if (c + 2 < NCH) tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 2) * 32), ra);
+    else release();
+    put(rb, c + 1);
+  }
+}
+
 template <int DT, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   TcParams p) {
+                   const __grid_constant__ EpiMaps em, TcParams p) {
   using C = Cfg<DT, BN, STAGES>;
   using T = typename C::T;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -617,6 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ epilogue ----------------------------------
     const int q = warp - 4;  // TMEM lane quadrant == warp % 4
     int local = 0;
+    int nst = 0;   // chunks this warp has stored through the TMA
+    unsigned char* epi = smem + C::EPI_OFF + q * C::EPI_BUFS * 4096;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int tm, tn;
       tile_coords(tile, p.tiles_m, tm, tn);
@@ -630,12 +706,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int col0 = tn * BN;
       const bool row_ok = row < p.N;
       uint32_t* yrow = reinterpret_cast<uint32_t*>(p.Y) + (size_t)row * p.M;
-      drain_quadrant<BN / 32>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_COLS), yrow, col0,
-                              p.M, row_ok, p.col_exp, p, row - lane, [&] {
-                                tc_fence_before();
-                                mbar_arrive(&bars->acc_empty[buf]);
-                              });
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * C::ACC_COLS);
+      auto release = [&] {
+        tc_fence_before();
+        mbar_arrive(&bars->acc_empty[buf]);
+      };
+      if (p.y_tma)
+        drain_quadrant_tma<BN / 32, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &em, nst);
+      else
+        drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release);
     }
+    // TMA stores still in flight complete before the CTA ends
+    if (p.y_tma && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -754,11 +837,13 @@ struct Cfg2 {
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
-  // unscaled kinds: 4 KB per epilogue warp to stage peer stores for the TMA
-  static constexpr bool PEER_TMA = !SCALED;
+  // unscaled kinds: TMA-store epilogue, 4 KB staging buffers per epilogue warp
+  // (two where the shared-memory budget allows, else one)
+  static constexpr bool EPI_TMA = !SCALED;
   static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
-  static constexpr int SMEM_BYTES = (PEER_TMA ? EPI_OFF + 4 * 4096 : BAR_OFF + 256) + 1024;
-  static constexpr int SMEM_BASE = BAR_OFF + 256 + 1024;   // launches without peer stores
+  static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448 ? 2 : 1;
+  static constexpr int SMEM_BYTES = (EPI_TMA ? EPI_OFF + 4 * EPI_BUFS * 4096 : BAR_OFF + 256) + 1024;
+  static constexpr int SMEM_BASE = BAR_OFF + 256 + 1024;   // launches with plain epilogue stores
   static constexpr uint32_t IDESC =
       SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
                 ((uint32_t)(256 >> 4) << 24))
@@ -777,7 +862,7 @@ template <int DT, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ PeerMaps pm,
+                        const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ EpiMaps pm,
                         TcParams p) {
   using C = Cfg2<DT, BN, STAGES>;
   using T = typename C::T;
@@ -950,6 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------ epilogue (both CTAs) ----------------------------
     const int q = warp - 4;
     int local = 0;
+    int nst = 0;   // chunks this warp has stored through the TMA
     for (int item = pair; item < num_items; item += npairs, ++local) {
       int tm, tn, half;
       item_coords(item, p, tm, tn, half);
@@ -970,14 +1056,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
       };
-      unsigned char* epi = C::PEER_TMA ? smem + C::EPI_OFF + q * 4096 : nullptr;
+      unsigned char* epi = C::EPI_TMA ? smem + C::EPI_OFF + q * C::EPI_BUFS * 4096 : nullptr;
+      if constexpr (C::EPI_TMA) {
+        if (p.y_tma) {
+          if (C::HALVES && half >= 0)
+            drain_quadrant_tma<BN / 64, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &pm, nst);
+          else
+            drain_quadrant_tma<BN / 32, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &pm, nst);
+          continue;
+        }
+      }
       if (C::HALVES && half >= 0)
         drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
       else
         drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
     }
-    // peer stores still in flight complete before the CTA ends
-    if (C::PEER_TMA && p.npeers && lane == 0) bulk_wait_all();
+    // TMA stores still in flight complete before the CTA ends
+    if (C::EPI_TMA && (p.npeers || p.y_tma) && lane == 0) bulk_wait_all();
     __syncwarp();
   }
 
@@ -1457,6 +1552,8 @@ int current_device() {
   return d;
 }
 
+bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
 // One-time set-up of a kernel per device (the dynamic shared-memory opt-in and,
 // for the pair kernel, its co-resident cluster count).  The lock keeps host
 // threads that launch on the same device at the same time from racing on it.
@@ -1511,6 +1608,18 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   set_peers(p, a);
   const int tiles = p.tiles_m * p.tiles_n;
   p.split_from = p.num_items = tiles;   // whole tiles only
+  // the TMA-store epilogue wherever Y's rows are whole 16-byte units
+  EpiMaps em;
+  std::memset(&em, 0, sizeof(em));
+  p.y_tma = (a.M % 4 == 0 && aligned(a.Y, 16)) ? 1 : 0;
+  if (p.y_tma) {
+    if (!make_map(&em.y, a.Y, CU_TENSOR_MAP_DATA_TYPE_UINT32, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.M * 4, 32, 32))
+      return cudaErrorInvalidValue;
+    for (int i = 0; i < a.npeers; ++i)
+      if (!make_map(&em.m[i], a.ypeers[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, (uint64_t)a.M, (uint64_t)a.N,
+                    (uint64_t)a.M * 4, 32, 32))
+        return cudaErrorInvalidValue;
+  }
   const int grid = tiles < a.num_sms ? tiles : a.num_sms;
   auto k = tc_gemm_kernel<DT, BN, STAGES>;
   static DevOnce once;   // per device: dynamic shared memory opt-in done
@@ -1518,12 +1627,12 @@ cudaError_t launch_cfg(const RunArgs& a, const void* W, const uint8_t* sfa = nul
   {
     std::lock_guard<std::mutex> lk(once.mu);
     if (!(once.mask & (1u << (dev & 31)))) {
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_EPI);
       if (e != cudaSuccess) return e;
       once.mask |= 1u << (dev & 31);
     }
   }
-  k<<<grid, kThreads, C::SMEM_BYTES, a.stream>>>(tmA, tmB, p);
+  k<<<grid, kThreads, p.y_tma ? C::SMEM_EPI : C::SMEM_BYTES, a.stream>>>(tmA, tmB, em, p);
   return cudaGetLastError();
 }
 
@@ -1621,13 +1730,17 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   const int rem = tiles % pairs;
   p.split_from = (C::HALVES && rem > 0 && 2 * rem <= pairs) ? tiles - rem : tiles;
   p.num_items = tiles + (tiles - p.split_from);
-  // peers' Y blocks as TMA store targets (rows of M 32-bit words, a multiple of 16 bytes)
-  PeerMaps pm;
+  // this GPU's and the peers' Y blocks as TMA store targets (rows of M 32-bit
+  // words, a multiple of 16 bytes)
+  EpiMaps pm;
   std::memset(&pm, 0, sizeof(pm));
-  const bool use_epi = C::PEER_TMA && a.npeers > 0 && a.M % 4 == 0;
+  const bool use_epi = C::EPI_TMA && a.M % 4 == 0 && aligned(a.Y, 16);
+  p.y_tma = use_epi ? 1 : 0;
   // the staging buffers are dynamic shared memory, requested only when used
   cfg.dynamicSmemBytes = use_epi ? C::SMEM_BYTES : C::SMEM_BASE;
   if (use_epi) {
+    if (!make_map(&pm.y, a.Y, CU_TENSOR_MAP_DATA_TYPE_UINT32, (uint64_t)a.M, (uint64_t)a.N, (uint64_t)a.M * 4, 32, 32))
+      return cudaErrorInvalidValue;
     for (int i = 0; i < a.npeers; ++i)
       if (!make_map(&pm.m[i], a.ypeers[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, (uint64_t)a.M, (uint64_t)a.N,
                     (uint64_t)a.M * 4, 32, 32))
@@ -1687,7 +1800,6 @@ cudaError_t launch_widen(const RunArgs& a) {
   return cudaGetLastError();
 }
 
-bool aligned(const void* p, unsigned a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
 }  // namespace
 

@@ -12,7 +12,10 @@
 //
 // Probe kinds (gemm_peak_probe): 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4
 // (E4M3 x E2M1, UE8M0 block 32), 4 mxf4 (E2M1 x E2M1, block 32), and
-// 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2, M = 256).
+// 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2, M = 256).  Kinds
+// 8 f16 / 9 i8 / 10 f8f6f4 are the pairs again with B read MN-major (the
+// instruction descriptor's transpose-B bit, 128-byte swizzle atoms along N),
+// the operand layout of the [K,M] weights in the GEMM's pair kernel.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -32,21 +35,33 @@ constexpr int kSfOff = kA + kB;           // 512 B of unit scale factors
 constexpr int kBarOff = kSfOff + 512;
 constexpr int kPeakSmem = kBarOff + 64 + 1024;
 
-template <int KIND, bool PAIR>
+template <int KIND, bool PAIR, bool BMN = false>
 constexpr uint32_t peak_idesc() {
   constexpr uint32_t m = PAIR ? 256u : 128u;   // a pair computes 256 rows; each CTA holds N/2 of B
   constexpr uint32_t n = (uint32_t)kPeakN;
-  if constexpr (KIND == kKindF16) return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
-  if constexpr (KIND == kKindI8) return (2u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
-  if constexpr (KIND == kKindF8F6F4) return (1u << 4) | ((n >> 3) << 17) | ((m >> 4) << 24);
+  constexpr uint32_t tb = BMN ? (1u << 16) : 0u;   // B MN-major
+  if constexpr (KIND == kKindF16) return (1u << 4) | tb | ((n >> 3) << 17) | ((m >> 4) << 24);
+  if constexpr (KIND == kKindI8)
+    return (2u << 4) | (1u << 7) | (1u << 10) | tb | ((n >> 3) << 17) | ((m >> 4) << 24);
+  if constexpr (KIND == kKindF8F6F4) return (1u << 4) | tb | ((n >> 3) << 17) | ((m >> 4) << 24);
   if constexpr (KIND == kKindMxF8F6F4)
     return (0u << 7) | (5u << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
   return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);   // mxf4
 }
 
-template <int KIND, bool PAIR>
+template <int KIND, bool PAIR, bool BMN = false>
 __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* sink, int* dev_err) {
   static_assert(!PAIR || KIND <= kKindF8F6F4, "pairs: unscaled kinds");
+  static_assert(!BMN || PAIR, "MN-major B: pair probes");
+  // MN-major B as the pair kernel lays it out: boxes of (128 bytes of N) x
+  // (one 128-byte K stage), the boxes kBox bytes apart (the descriptor's
+  // leading-dimension offset); one MMA's K slice starts kAdv bytes further on
+  constexpr int kEs = KIND == kKindF16 ? 2 : 1;
+  constexpr uint32_t kBoxMn = 128 / kEs;                     // N elements per box
+  constexpr uint32_t kBoxK = 128 / kEs;                      // K elements per stage
+  constexpr uint32_t kBox = kBoxK * 128;                     // bytes per box
+  constexpr uint32_t kAdv = (32 / kEs) * 128;                // K rows of one MMA x 128 B
+  static_assert(!BMN || (kPeakN / 2 / kBoxMn) * kBox <= (uint32_t)kB, "B boxes fit the B tile");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -86,7 +101,7 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* 
   const bool leader = !PAIR || cluster_ctarank() == 0;
 
   if (warp == 0 && lane == 0 && leader) {
-    constexpr uint32_t idesc = peak_idesc<KIND, PAIR>();
+    constexpr uint32_t idesc = peak_idesc<KIND, PAIR, BMN>();
     const uint32_t a = smem_u32(smem), b = a + kA, sf = a + kSfOff;
     const uint32_t sfa_t = tmem + kPeakN, sfb_t = tmem + kPeakN + 4;
     if constexpr (KIND >= kKindMxF8F6F4) {
@@ -97,7 +112,7 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* 
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint64_t ad = sdesc_sw128(a + kk * 32, 16, 1024);
-        const uint64_t bd = sdesc_sw128(b + kk * 32, 16, 1024);
+        const uint64_t bd = BMN ? sdesc_sw128(b + kk * kAdv, kBox, 1024) : sdesc_sw128(b + kk * 32, 16, 1024);
         const uint32_t acc = (r | kk) != 0 ? 1u : 0u;
         if constexpr (PAIR) tc_mma_pair<KIND>(tmem, ad, bd, idesc, acc);
         else if constexpr (KIND >= kKindMxF8F6F4) tc_mma_bs<KIND>(tmem, ad, bd, idesc, acc, sfa_t, sfb_t);
@@ -125,9 +140,9 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* 
   }
 }
 
-template <int KIND, bool PAIR>
+template <int KIND, bool PAIR, bool BMN = false>
 cudaError_t launch_one(int reps, int ctas, float* sink, int* dev_err, cudaStream_t st) {
-  auto k = peak_kernel<KIND, PAIR>;
+  auto k = peak_kernel<KIND, PAIR, BMN>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -150,7 +165,7 @@ cudaError_t launch_one(int reps, int ctas, float* sink, int* dev_err, cudaStream
 // K elements per tcgen05.mma by probe kind
 static int peak_kmma(int kind) {
   switch (kind) {
-    case 0: case 5: return 16;
+    case 0: case 5: case 8: return 16;
     case 4: return 64;
     default: return 32;
   }
@@ -173,6 +188,9 @@ cudaError_t launch_peak(int kind, int reps, int ctas, float* sink, int* dev_err,
     case 5: return launch_one<kKindF16, true>(reps, ctas, sink, dev_err, st);
     case 6: return launch_one<kKindI8, true>(reps, ctas, sink, dev_err, st);
     case 7: return launch_one<kKindF8F6F4, true>(reps, ctas, sink, dev_err, st);
+    case 8: return launch_one<kKindF16, true, true>(reps, ctas, sink, dev_err, st);
+    case 9: return launch_one<kKindI8, true, true>(reps, ctas, sink, dev_err, st);
+    case 10: return launch_one<kKindF8F6F4, true, true>(reps, ctas, sink, dev_err, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -230,7 +230,9 @@ int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const voi
 
 /* ---- pure-compute peak probe (tune/peak.metal + tune/peak.swift) ------------ */
 /* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4, and
- * 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2).  Runs 2 untimed and
+ * 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2); 8 f16 / 9 i8 /
+ * 10 f8f6f4 on CTA pairs with B read MN-major (the layout of [K,M] weights,
+ * as the GEMM's pair tiles read W).  Runs 2 untimed and
  * `iters` timed launches of a kernel that issues reps x 4 tcgen05.mma
  * (128 x 256 per CTA, or 256 x 256 per pair) on operands resident in shared
  * memory, no global traffic in the loop (tune/peak.metal:29-87), and
