@@ -49,7 +49,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -156,80 +155,125 @@ REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0
                "applications_clocks_setting": 0x2, "sync_boost": 0x10}
 
 
+# The sampler runs in its own process: it polls NVML every 0.2 ms and writes
+# "monotonic-time sm_mhz reason-bits" lines to a file, independently of this
+# process's threads (a Python thread would be starved by the interpreter lock
+# during short timed regions).  Windows are matched by CLOCK_MONOTONIC, which
+# is system-wide on Linux.
+_SAMPLER = r"""
+import sys, time
+try:
+    import pynvml as N
+    N.nvmlInit()
+    h = N.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+    print("max", N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM), flush=True)
+    while True:
+        t = time.monotonic()
+        m = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+        b = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+        print("%.6f %d %d" % (t, m, b), flush=True)
+        time.sleep(0.0002)
+except Exception as e:
+    print("error", str(e).replace(chr(10), " "), flush=True)
+"""
+
+
 class ClockSampler:
-    """NVML SM clock and throttle reasons, polled every 0.5 ms by a thread
-    that keeps a sample only while a timed GPU region is open (`window`)."""
+    """NVML SM clock and throttle reasons of one GPU, sampled by a child
+    process every 0.2 ms for the whole run; `window()` marks a timed region
+    and summarises the samples taken inside it."""
 
     def __init__(self, index):
         self.index = index
-        self.samples = []        # (sm_mhz, reason bits)
-        self.active = False
-        self.max_mhz = None
+        self.proc = None
+        self.path = None
         self.err = None
-        self._stop = threading.Event()
-        self._t = None
 
     def __enter__(self):
+        import subprocess
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="clk", suffix=".txt")
         try:
-            import pynvml as N
-            N.nvmlInit()
-            self._N = N
-            self._h = N.nvmlDeviceGetHandleByIndex(self.index)
-            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self._h, N.NVML_CLOCK_SM)
-        except Exception as e:   # NVML missing: report it, never fail the bench
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, str(self.index)], stdout=fd,
+                                         stderr=subprocess.DEVNULL)
+        except OSError as e:
             self.err = str(e)
-            return self
-        self._t = threading.Thread(target=self._run, daemon=True)
-        self._t.start()
+        os.close(fd)
+        # wait (bounded) for the first sample so the first window is covered
+        t0 = time.monotonic()
+        while self.proc is not None and time.monotonic() - t0 < 20.0:
+            if len(self._lines()) >= 2 or self.proc.poll() is not None:
+                break
+            time.sleep(0.01)
         return self
 
-    def _run(self):
-        N = self._N
-        while not self._stop.is_set():
-            if self.active:
-                try:
-                    mhz = N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM)
-                    bits = N.nvmlDeviceGetCurrentClocksEventReasons(self._h)
-                    self.samples.append((mhz, bits))
-                except Exception as e:
-                    self.err = str(e)
-                    break
-            time.sleep(0.0005)
-
     def __exit__(self, *a):
-        self._stop.set()
-        if self._t:
-            self._t.join(timeout=2)
+        if self.proc is not None and self.proc.poll() is None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def _lines(self):
+        try:
+            with open(self.path) as f:
+                return f.read().splitlines()
+        except OSError:
+            return []
+
+    def _parse(self):
+        mx, samples, err = None, [], self.err
+        for ln in self._lines():
+            parts = ln.split()
+            if not parts:
+                continue
+            if parts[0] == "max":
+                mx = int(parts[1])
+            elif parts[0] == "error":
+                err = ln[6:]
+            elif len(parts) == 3:
+                try:
+                    samples.append((float(parts[0]), int(parts[1]), int(parts[2])))
+                except ValueError:
+                    pass   # a line still being written
+        return mx, samples, err
 
     class _Window:
         def __init__(self, clk):
             self.clk = clk
+            self.t0 = self.t1 = None
 
         def __enter__(self):
-            self.i0 = len(self.clk.samples)
-            self.clk.active = True
+            self.t0 = time.monotonic()
             return self
 
         def __exit__(self, *a):
-            self.clk.active = False
-            self.i1 = len(self.clk.samples)
+            self.t1 = time.monotonic()
 
         def summary(self):
-            return self.clk.summary(self.i0, self.i1)
+            return self.clk.summary(self.t0, self.t1)
 
     def window(self):
         return ClockSampler._Window(self)
 
-    def summary(self, i0=0, i1=None):
-        s = self.samples[i0:i1]
+    def summary(self, t0=None, t1=None, windows=None):
+        """Samples between t0 and t1 (the whole run when both are None), or
+        inside any of `windows` (a list of (t0, t1))."""
+        mx, samples, err = self._parse()
+        if windows is not None:
+            s = [(m, b) for t, m, b in samples if any(a <= t <= z for a, z in windows)]
+        else:
+            s = [(m, b) for t, m, b in samples if (t0 is None or t >= t0) and (t1 is None or t <= t1)]
         bits = 0
         for _, b in s:
             bits |= b
         d = {"sm_mhz": statistics.median([m for m, _ in s]) if s else None,
-             "sm_min_mhz": min((m for m, _ in s), default=None), "sm_max_mhz": self.max_mhz,
-             "reasons": sorted(k for k, v in REASON_BITS.items() if bits & v), "samples": len(s)}
-        if self.err:
-            d["error"] = self.err
+             "sm_min_mhz": min((m for m, _ in s), default=None), "sm_max_mhz": mx,
+             "reasons": sorted(k for k, v in REASON_BITS.items() if bits & v), "samples": len(s),
+             "source": "NVML in a sampler process, every 0.2 ms, samples inside the timed region"}
+        if err:
+            d["error"] = err
         return d
 
 
@@ -390,6 +434,7 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
     from mlpgemm.data import Operands
     names = G.tile_names()
     rows = []
+    windows = []
     shared_w = {}
     for sname, N, K, M, iters in SUITE:
         ops = Operands(N, K, M, "seeded", 0)
@@ -425,6 +470,7 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
                 kind_probe = "mxf8f6f4"
             else:
                 kind_probe = kind
+            windows.append((w.t0, w.t1))
             row = {"shape": sname, "dtype": dtype, "N": N, "K": K, "M": M, "tile": tile,
                    "ms_median": med, "ms_mean": statistics.mean(ms), "iters": iters,
                    "value": flops / (med / 1e3) / 1e12, "unit": unit_of(dtype),
@@ -444,7 +490,7 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
             del d
         if sname == "fat":
             shared_w = {k: v for k, v in ops._cache.items() if k.startswith("w")}
-    return rows
+    return rows, windows
 
 
 def e2e_measure(G, dev, dt, ti, ops, dtype, W, WS, Y, WSP, wsb, N, K, width, a, d):
@@ -489,6 +535,8 @@ def ours(a):
     torch = dist = None
     if world > 1:
         import datetime
+        # NCCL's banner would otherwise share stdout with the JSON line
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
 
         import torch
         import torch.distributed as dist
@@ -650,13 +698,13 @@ def ours(a):
             line["probe"]["what"] = "gemm_peak_probe: tcgen05 MMAs on operands resident in shared memory, 1 CTA/SM"
             if not a.no_suite:
                 del d, X, W, Y, WSP
-                suite = run_suite(G, clk, FL, probe, hbm, bf16, src)
+                suite, windows = run_suite(G, clk, FL, probe, hbm, bf16, src)
                 line["suite"] = {"rows": suite, "n": len(suite), "parity_ok": all(r["parity_ok"] for r in suite),
                                  "what": ("every dtype x shape of the reference's suite (main.swift:156-160), "
                                           "default tile, L2 flushed before every timed launch, median of the "
                                           "CUDA-event times; frac = of the measured per-kind peak (thin rows: "
                                           "of the measured HBM copy bandwidth), probe_frac = of gemm_peak_probe"),
-                                 "clocks": clk.summary()}
+                                 "clocks": clk.summary(windows=windows)}
                 ok = ok and line["suite"]["parity_ok"]
     if world == 1 and not a.no_cpu_baseline:
         v, rows, thr, el = cpu_sample(dtype, ops, seconds=10.0)

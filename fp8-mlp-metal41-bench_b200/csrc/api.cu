@@ -256,10 +256,11 @@ int gemm_check_layout(int dtype, int N, int K, int M) {
 int gemm_default_tile(int dtype, int N, int K, int M) {
   if (layout_check(dtype, N, K, M) != GEMM_OK) return -1;
   if (N > 16) {
-    // block-scaled kinds: the 1-CTA 128x256 tile measures ahead of the CTA pair
-    // (which keeps one accumulator in TMEM next to its scale cells)
+    // block-scaled kinds: the CTA pair (TMA-store epilogue) measures 2-5 % ahead
+    // of the 1-CTA 128x256 tile from N = 256 on; below that the pair's second
+    // CTA would hold no rows
     const bool scaled = dtype == kMX4X4 || dtype == kMX8X4 || dtype == kF8X4;
-    if (scaled && tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
+    if (scaled && N < 256 && tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");
     // A16 kinds on the pair tile widen all of W to f16 first: worth it once the
     // per-128-row conversions of the 1-CTA tiles would repeat (N >= 256)
     const bool a16 = dtype == kINT8 || dtype == kFP8 || dtype == kMXFP4;

@@ -65,11 +65,6 @@ constexpr int kSfChunk = 512;    // one 32 x 16-byte scale-factor block (one tcg
 template <int DT>
 struct Traits;
 
-// f4f4 on CTA pairs: kind::f8f6f4 with E2M1 x E2M1 (no scales), both
-// operands K-major (W transposed to [M,K] first) and unpacked by TMA into
-// 8-bit containers in shared memory (16U4_ALIGN16B).
-constexpr int kF4F4Pair = 64;
-
 template <>
 struct Traits<kFP16> {
   static constexpr int kind = kKindF16, a_bits = 16, b_bits = 16, nsf = 0;
@@ -105,12 +100,6 @@ struct Traits<kMX8X4> {
   static constexpr int kind = kKindMxF8F6F4, a_bits = 8, b_bits = 8, nsf = 1;
   static constexpr bool b_mn = false, x_plane = true, w_plane = true, b_unpack4 = true;
   static constexpr uint32_t a_fmt = 0, b_fmt = 5, c_fmt = 1;  // E4M3, E2M1
-};
-template <>
-struct Traits<kF4F4Pair> {
-  static constexpr int kind = kKindF8F6F4, a_bits = 8, b_bits = 8, nsf = 0;
-  static constexpr bool b_mn = false, x_plane = false, w_plane = false, b_unpack4 = true;
-  static constexpr uint32_t a_fmt = 5, b_fmt = 5, c_fmt = 1;  // E2M1, E2M1 -> F32
 };
 template <>
 struct Traits<kF8X4> {
@@ -805,11 +794,10 @@ struct Cfg2 {
   static constexpr int A_BYTES = kBM * kRowBytes;
   static constexpr int B_BYTES = BH * kRowBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // 4-bit operands unpacked into 8-bit containers by TMA (16U4_ALIGN16B); those
-  // loads count the packed source bytes, half of what they write
-  static constexpr bool A_UNPACK = DT == kF4F4Pair;
-  static constexpr bool B_UNPACK = DT == kF4F4Pair || T::b_unpack4;
-  static constexpr int STAGE_TX = (A_UNPACK ? A_BYTES / 2 : A_BYTES) + (B_UNPACK ? B_BYTES / 2 : B_BYTES);
+  // 4-bit W unpacked into 8-bit containers by TMA (16U4_ALIGN16B); those loads
+  // count the packed source bytes, half of what they write
+  static constexpr bool B_UNPACK = T::b_unpack4;
+  static constexpr int STAGE_TX = A_BYTES + (B_UNPACK ? B_BYTES / 2 : B_BYTES);
   // block-scaled kinds: per stage SF_CELLS 512-byte scale blocks for this CTA's
   // 128 rows of A and for all BN columns of B (each CTA's TMEM holds the scales
   // of every column the pair's MMA multiplies its rows with), as in Cfg
@@ -837,11 +825,14 @@ struct Cfg2 {
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
-  // unscaled kinds: TMA-store epilogue, 4 KB staging buffers per epilogue warp
-  // (two where the shared-memory budget allows, else one)
-  static constexpr bool EPI_TMA = !SCALED;
+  // TMA-store epilogue: 4 KB staging buffers per epilogue warp, two where the
+  // shared-memory budget allows, else one; none (plain stores) if even one
+  // does not fit beside the ring
   static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
-  static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448 ? 2 : 1;
+  static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448   ? 2
+                                  : EPI_OFF + 4 * 1 * 4096 + 1024 <= 232448 ? 1
+                                                                            : 0;
+  static constexpr bool EPI_TMA = EPI_BUFS > 0;
   static constexpr int SMEM_BYTES = (EPI_TMA ? EPI_OFF + 4 * EPI_BUFS * 4096 : BAR_OFF + 256) + 1024;
   static constexpr int SMEM_BASE = BAR_OFF + 256 + 1024;   // launches with plain epilogue stores
   static constexpr uint32_t IDESC =
@@ -850,7 +841,7 @@ struct Cfg2 {
              : ((T::c_fmt << 4) | (T::a_fmt << 7) | (T::b_fmt << 10) | ((T::b_mn ? 1u : 0u) << 16) |
                 ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24));
   // half tiles (256 x BN/2): unscaled kinds without 4-bit unpacking
-  static constexpr bool HALVES = !SCALED && !A_UNPACK && !B_UNPACK && (!T::b_mn || (BH / 2) % B_BOX_MN == 0);
+  static constexpr bool HALVES = !SCALED && !B_UNPACK && (!T::b_mn || (BH / 2) % B_BOX_MN == 0);
   static constexpr int STAGE_TX_H = A_BYTES + B_BYTES / 2;
   static constexpr uint32_t IDESC_H = (IDESC & ~(0x3Fu << 17)) | ((uint32_t)(BN / 2 >> 3) << 17);
   static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
@@ -934,9 +925,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // just complete their transactions on the leader's barrier (a remote
         // arrive per stage would put a cross-SM round trip in the peer's loop).
         if (rank == 0) mbar_arrive_expect_tx(&bars->full[stage], 2 * stx);
-        // x counts elements of the map: 16-bit or 4-bit (unpacking maps) elements, else bytes
+        // x counts elements of the map: 16-bit elements, else bytes
         tma_load_2d_pair(a_dst, &tmA, lfull,
-                         kb * ((T::a_bits == 16 || C::A_UNPACK) ? C::K_PER_STAGE : kRowBytes),
+                         kb * (T::a_bits == 16 ? C::K_PER_STAGE : kRowBytes),
                          tm * 256 + (int)rank * kBM);
         if constexpr (C::SCALED) {
           // packed scale blocks: rows of 512 bytes, [128-row tile][stage][cell]
@@ -1644,11 +1635,7 @@ cudaError_t launch_pair(const RunArgs& a, const void* W, const uint8_t* sfa = nu
   CUtensorMap tmA, tmB, tmSA, tmSB;
   const CUtensorMapDataType ty8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   bool ok;
-  if constexpr (C::A_UNPACK) {
-    // packed E2M1 rows of K/2 bytes, unpacked to one byte per element in shared memory
-    ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, (uint64_t)a.K, (uint64_t)a.N,
-                  (uint64_t)a.K / 2, C::K_PER_STAGE, kBM);
-  } else if constexpr (T::a_bits == 16) {
+  if constexpr (T::a_bits == 16) {
     ok = make_map(&tmA, a.X, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K * 2,
                   C::K_PER_STAGE, kBM);
   } else {
@@ -1895,7 +1882,7 @@ cudaError_t launch_scaled(const RunArgs& a) {
 // kernel; each CTA brings its own rows' X scales and all 256 columns' W scales.
 template <int DT>
 cudaError_t launch_scaled_pair(const RunArgs& a) {
-  constexpr int kStagesPair = 6;
+  constexpr int kStagesPair = 5;   // 5 x 35 KB leaves room for the TMA-store staging buffers
   const ScaledWs w = scaled_ws(DT, 256, a.N, a.K, a.M);
   if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
   uint8_t* base = static_cast<uint8_t*>(a.ws);
@@ -1914,8 +1901,8 @@ cudaError_t launch_scaled_pair(const RunArgs& a) {
                                            w.b_tiles * w.stages * w.cells);
 }
 
-// f4f4 on CTA pairs: transpose W to [M,K] into the workspace, then
-// kind::f8f6f4 (E2M1 x E2M1) over both operands unpacked by TMA.
+// f4f4 on CTA pairs: transpose W to [M,K] into the workspace (the 4-bit MMA
+// operands are K-major), then kind::mxf4 (E2M1 x E2M1) with unit scales.
 cudaError_t launch_f4f4_pair(const RunArgs& a) {
   const ScaledWs w = scaled_ws(kF4F4, 256, a.N, a.K, a.M);
   if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
@@ -1924,7 +1911,9 @@ cudaError_t launch_f4f4_pair(const RunArgs& a) {
   transpose_fp4_kernel<<<grid, 256, 0, a.stream>>>(static_cast<const uint8_t*>(a.W), wt, a.K, a.M);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return launch_pair<kF4F4Pair, 256, 6>(a, wt);
+  // kind::mxf4 with unit scales (no scale planes: the kernel's block of UE8M0
+  // 127s), on packed E2M1 straight from shared memory
+  return launch_pair<kF4F4, 256, 5>(a, wt);
 }
 
 }  // namespace

@@ -876,6 +876,154 @@ __global__ void __launch_bounds__(kThreads, NR == 1 ? 4 : 2) gemv_km_kernel(Gemv
 }
 
 // ---------------------------------------------------------------------------
+// [M,K] weights, thin rows (N <= 2), one K split: every lane keeps BPL weight
+// blocks in flight from the start to the end of the row.
+// ---------------------------------------------------------------------------
+// At the suite's thin row (K = 4096, M = 11008) the whole weight stream is
+// 24 MB, a few microseconds of HBM time, so a kernel whose threads wait for
+// several dependent load rounds stays latency-bound.  Here a CTA is 4 warps;
+// a warp owns 4 weight rows (output columns) and 8 lanes share a row as in
+// gemv_km_kernel: lane j takes the row's 16-byte blocks j, j + 8, j + 16, ...
+// (each warp instruction reads 128 contiguous bytes of 4 rows).  A lane
+// issues its first BPL blocks before it stages X, and each register is
+// reloaded with the block BPL positions further on as soon as its block has
+// been used, so BPL blocks stay in flight per lane until the row ends.  With
+// 128-thread CTAs, 5 per SM, the thin row's 688 CTAs are resident at once.
+// The arithmetic and its order are gemv_km_kernel's: per block the exact f16
+// products summed in f32, times 2^(sw-127) * 2^(sx-127); the 8 lanes of a row
+// reduced by the same butterfly; so the results are identical bit for bit.
+constexpr int kWideThreads = 128;
+constexpr int kWideRowsPerCta = (kWideThreads / 32) * 4;
+
+template <int DT, int NR, int BPL>
+__global__ void __launch_bounds__(kWideThreads, 5) gemv_km_wide_kernel(GemvParams p) {
+  constexpr int LPR = 8;              // lanes per weight row
+  constexpr int XB = 40;              // f16 slots per 32-element block (80 bytes)
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int kbpr = p.K / 32;          // blocks per weight row (K % 32 == 0)
+  __half* xs = reinterpret_cast<__half*>(smem_raw);                              // [NR][kbpr][XB]
+  float* xsc = reinterpret_cast<float*>(smem_raw + (size_t)NR * kbpr * XB * 2);  // [NR][kbpr]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane / LPR, j = lane % LPR;
+  const int n0 = blockIdx.z * NR;
+  const int m = blockIdx.x * kWideRowsPerCta + warp * 4 + r;
+  const bool mok = m < p.M;
+  const uint8_t* wrow = reinterpret_cast<const uint8_t*>(p.W) + (size_t)(mok ? m : 0) * (p.K / 2);
+  const uint8_t* srow = p.wscale + (size_t)(mok ? m : 0) * kbpr;
+  const int nblk = (kbpr - j + LPR - 1) / LPR;   // blocks of this lane: j + LPR * i, i < nblk
+
+  uint4 w[BPL];
+  uint32_t sc[BPL];
+  auto fetch = [&](int u, int i) {   // block i of this lane into slot u
+    if (mok && i < nblk) {
+      const int blk = j + LPR * i;
+      w[u] = __ldcs(reinterpret_cast<const uint4*>(wrow + (size_t)blk * 16));
+      sc[u] = __ldg(srow + blk);
+    } else {
+      w[u] = make_uint4(0, 0, 0, 0);
+      sc[u] = 0;
+    }
+  };
+#pragma unroll
+  for (int u = 0; u < BPL; ++u) fetch(u, u);   // the weights are requested before X is staged
+
+  // X as unscaled f16 (exact), zero past N, 16 bytes of X per load
+  for (int n = 0; n < NR; ++n) {
+    const bool nok = n0 + n < p.N;
+    const size_t row0 = (size_t)(nok ? n0 + n : 0) * p.K;
+    if constexpr (x_is_half(DT)) {
+      for (int e = tid * 8; e < p.K; e += kWideThreads * 8) {   // 8 halves
+        const uint4 v = nok ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.X) + row0 + e))
+                            : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(xs + ((size_t)n * kbpr + e / 32) * XB + e % 32) = v;
+      }
+    } else if constexpr (x_is_e4m3(DT)) {
+      for (int e = tid * 16; e < p.K; e += kWideThreads * 16) {   // 16 E4M3 bytes
+        const uint4 v = nok ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.X) + row0 + e))
+                            : make_uint4(0, 0, 0, 0);
+        const uint32_t b[4] = {v.x, v.y, v.z, v.w};
+        uint32_t h[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          h[2 * q] = e4m3x2_to_h2(b[q] & 0xFFFFu);
+          h[2 * q + 1] = e4m3x2_to_h2(b[q] >> 16);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(xs + ((size_t)n * kbpr + e / 32) * XB + e % 32);
+        dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+        dst[1] = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+    } else {
+      for (int e = tid * 32; e < p.K; e += kWideThreads * 32) {   // one block of 32 E2M1
+        const uint4 v = nok ? __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.X) + (row0 + e) / 2))
+                            : make_uint4(0, 0, 0, 0);
+        const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+        uint4* dst = reinterpret_cast<uint4*>(xs + ((size_t)n * kbpr + e / 32) * XB);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t t4[4];
+          e2m1x8_to_h2(words[q], t4);
+          dst[q] = make_uint4(t4[0], t4[1], t4[2], t4[3]);
+        }
+      }
+    }
+  }
+  for (int i = tid; i < NR * kbpr; i += kWideThreads) {
+    const int n = i / kbpr, blk = i % kbpr;
+    float s = 1.f;
+    if constexpr (x_scaled(DT)) {
+      if (n0 + n < p.N) s = dec_ue8m0(p.xscale[(size_t)(n0 + n) * kbpr + blk]);
+    }
+    xsc[i] = s;
+  }
+  __syncthreads();
+
+  float acc[NR];
+#pragma unroll
+  for (int n = 0; n < NR; ++n) acc[n] = 0.f;
+  for (int i0 = 0; i0 < nblk; i0 += BPL) {
+#pragma unroll
+    for (int u = 0; u < BPL; ++u) {
+      const int i = i0 + u;
+      if (i < nblk) {
+        const int bl = j + LPR * i;
+        uint32_t h[16];
+        const uint32_t words[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t t4[4];
+          e2m1x8_to_h2(words[q], t4);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) h[4 * q + t] = t4[t];
+        }
+        const float ws = dec_ue8m0(sc[u]);
+#pragma unroll
+        for (int n = 0; n < NR; ++n) {
+          const uint4* xq = reinterpret_cast<const uint4*>(xs + ((size_t)n * kbpr + bl) * XB);
+          float d = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 xv = xq[q];
+            fma2_dot(d, h[4 * q + 0], xv.x);
+            fma2_dot(d, h[4 * q + 1], xv.y);
+            fma2_dot(d, h[4 * q + 2], xv.z);
+            fma2_dot(d, h[4 * q + 3], xv.w);
+          }
+          acc[n] = fmaf(d, ws * xsc[n * kbpr + bl], acc[n]);
+        }
+      }
+      fetch(u, i + BPL);   // the slot's next block (a no-op past the row's end)
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NR; ++n) {
+    float v = acc[n];
+#pragma unroll
+    for (int o = 1; o < LPR; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (j == 0 && mok && n0 + n < p.N) reinterpret_cast<float*>(p.Y)[(size_t)(n0 + n) * p.M + m] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 template <int DT>
@@ -1083,6 +1231,29 @@ size_t gemv_workspace(int dt, int ksplit, int N, int K, int M) {
   return kCounterBytes + (size_t)eff * N * M * 4;
 }
 
+// The [M,K] thin-row kernel with all of a lane's blocks in flight (N <= 2,
+// one K split).
+template <int DT>
+cudaError_t launch_km_wide(const GemvParams& p, cudaStream_t st) {
+  const int nr = p.N <= 1 ? 1 : 2;
+  const size_t smem = (size_t)nr * (p.K / 32) * (80 + 4);
+  if (smem > kMaxGemvSmem) return cudaErrorInvalidValue;
+  const dim3 grid((p.M + kWideRowsPerCta - 1) / kWideRowsPerCta, 1, (p.N + nr - 1) / nr);
+  auto launch = [&](auto k) -> cudaError_t {
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+    }
+    k<<<grid, kWideThreads, smem, st>>>(p);
+    return cudaGetLastError();
+  };
+  return nr == 1 ? launch(gemv_km_wide_kernel<DT, 1, 8>) : launch(gemv_km_wide_kernel<DT, 2, 8>);
+}
+
+static bool km_wide(int dt, int N, int ksplit, const void* X) {
+  return w_is_mx(dt) && N <= 2 && ksplit == 1 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0;
+}
+
 cudaError_t launch_gemv(const RunArgs& a, int ksplit) {
   if (ksplit < 1) ksplit = 1;
   GemvParams p;
@@ -1111,6 +1282,17 @@ cudaError_t launch_gemv(const RunArgs& a, int ksplit) {
   }
   p.stream = 0;
   p.nslabs = p.units_per_slab = p.total_units = 0;
+  // the [M,K] kernels read W in 16-byte blocks
+  if (w_is_mx(a.dt) && (reinterpret_cast<uintptr_t>(a.W) & 15u) != 0) return cudaErrorInvalidValue;
+  if (km_wide(a.dt, a.N, p.ksplit, a.X)) {
+    switch (a.dt) {
+      case kMXFP4: return launch_km_wide<kMXFP4>(p, a.stream);
+      case kMX4X4: return launch_km_wide<kMX4X4>(p, a.stream);
+      case kMX8X4: return launch_km_wide<kMX8X4>(p, a.stream);
+      case kF8X4: return launch_km_wide<kF8X4>(p, a.stream);
+      default: break;
+    }
+  }
   return launch_any(a.dt, p, grid, nr, a.num_sms, a.stream);
 }
 

@@ -295,8 +295,8 @@ def test_e2e_timing_moves_the_result(gemm, dtype):
 
 @pytest.mark.parametrize("M", [512, 258])
 def test_f4f4_pair_ragged_m(gemm, M):
-    # W [K,M] packed along M is transposed to [M,K] (any even M) and TMA unpacks
-    # E2M1 for kind::f8f6f4
+    # W [K,M] packed along M is transposed to [M,K] (any even M) for the
+    # K-major 4-bit operands of kind::mxf4 (unit scales)
     N, K = 384, 1024
     out, ref, _ = run_case(gemm, "f4f4", "256x256", N, K, M)
     assert_close("f4f4", out, ref)
