@@ -12,8 +12,8 @@ against the oracle (main.swift:560-594, tightened to fp64 / int64):
     sides) plus 32 seeded random rows, each over ALL M columns, so that
     every column tile, the ragged last column tile and the last wave's
     half tiles are inside the check;
-  * whole outputs for the two configurations the bench's headline reads
-    (i8i8 square and f8f8 fat).
+  * whole outputs for i8i8 square (the integer configuration) and f8f8 fat
+    (the configuration of the bench's headline).
 
 Bar: i8i8 bit-exact; float dtypes max relative error <= 1e-3 with the
 denominator max(|ref|, 1e-2 * rms(ref)).  The unfloored max relative error
