@@ -224,7 +224,10 @@ int gemm_launches_per_run(int dtype, int tile, int N, int K, int M);
  * GEMM_ERR_ARGS.  The first call on a device looks up the array's address on
  * that device; make it before any stream capture.  All calls share the array
  * (each clears its counters first): calls that overlap on the GPU race and
- * must be serialised by the caller.  Calls no cudaMalloc / cudaFree. */
+ * must be serialised by the caller.  Calls no cudaMalloc / cudaFree.  A split
+ * the kernel cannot take (shared memory, or more split-K tiles than the counter
+ * region holds) returns GEMM_ERR_ARGS with the reason; the caller's current
+ * device is the same on return. */
 int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const void *W, void *Y,
                      int N, int K, int M, const void *xscale, const void *wscale, void *stream);
 
