@@ -73,6 +73,7 @@ struct TileDef {
 };
 const TileDef kTiles[] = {
     {"256x256", kTileTC, 256, 256},  {"128x256", kTileTC, 256, 128}, {"128x128", kTileTC, 128, 128},
+    {"256x192", kTileTC, 192, 256},
     {"16x128", kTileThin, 0, 0},     {"stream", kTileStream, 0, 0},
     {"gemv.k1", kTileGemv, 1, 0},    {"gemv.k2", kTileGemv, 2, 0},   {"gemv.k4", kTileGemv, 4, 0},
     {"gemv.k8", kTileGemv, 8, 0},    {"gemv.k16", kTileGemv, 16, 0}, {"gemv.k32", kTileGemv, 32, 0},

@@ -247,31 +247,38 @@ __device__ __forceinline__ void item_coords(int i, const TcParams& p, int& tm, i
 // operand.
 struct SfPackJob {
   const uint8_t* plane;   // [rows, kbpr]
-  uint8_t* out;           // [tiles][stages][4][512]
-  int rows, tiles;
+  uint8_t* out;           // [tiles][stages][cells][512]
+  int rows, tiles;        // tiles: packed 128-row blocks (chunks) in all
+  int tile_rows;          // operand rows per MMA tile (128, 192 or 256)
+  int chunks;             // 128-row chunks per MMA tile: ceil(tile_rows / 128)
 };
 
 __global__ void __launch_bounds__(256) sf_pack_kernel(SfPackJob ja, SfPackJob jb, int kbpr, int stages, int nb,
                                                       int cells) {
-  const SfPackJob& j = blockIdx.y == 0 ? ja : jb;        // y = 0: X plane, 1: W plane
-  if (j.plane == nullptr) return;
+  const SfPackJob& job = blockIdx.y == 0 ? ja : jb;      // y = 0: X plane, 1: W plane
+  if (job.plane == nullptr) return;
   const int tid = blockIdx.x * 256 + threadIdx.x;       // one thread per (t, st, g, r0)
   const int r0 = tid & 31;
   const int g = (tid >> 5) % cells;
   const int rest = (tid >> 5) / cells;
   const int st = rest % stages, t = rest / stages;
-  if (t >= j.tiles) return;
-  const uint8_t* plane = j.plane;
-  const int rows = j.rows;
-  uint8_t* out = j.out;
+  if (t >= job.tiles) return;
+  const uint8_t* plane = job.plane;
+  const int rows = job.rows;
+  uint8_t* out = job.out;
+  // packed block t is chunk c of MMA tile t_outer: rows t_outer * tile_rows + 128 c + ...
+  const int t_outer = t / job.chunks, c = t % job.chunks;
+  const int tile_rows = job.tile_rows;
   uint32_t w[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int row = t * 128 + r0 + 32 * j;
+    const int row_in = c * 128 + r0 + 32 * j;   // row within the MMA tile
+    const int row = t_outer * tile_rows + row_in;
     uint32_t v = 0;
     for (int q = 0; q < 4; ++q) {
       const int kblk = st * nb + 4 * g + q;
-      const uint32_t sc = (row < rows && kblk < kbpr) ? plane[(size_t)row * kbpr + kblk] : 127u;
+      const uint32_t sc =
+          (row_in < tile_rows && row < rows && kblk < kbpr) ? plane[(size_t)row * kbpr + kblk] : 127u;
       v |= sc << (8 * q);
     }
     w[j] = v;
@@ -803,14 +810,16 @@ struct Cfg2 {
   // of every column the pair's MMA multiplies its rows with), as in Cfg
   static constexpr bool SCALED = T::nsf > 0;
   static constexpr int SF_CELLS = SCALED ? (kRowBytes / 32) * T::nsf / 4 : 0;
-  static constexpr int SF_B_CHUNKS = BN / 128;
+  static constexpr int SF_B_CHUNKS = (BN + 127) / 128;   // 128-row scale chunks of the B tile
   static constexpr int SF_A_BYTES = SF_CELLS * kSfChunk;
   static constexpr int SF_B_BYTES = SF_CELLS * SF_B_CHUNKS * kSfChunk;
   static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
   static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
-  // one accumulator when scaled: two 256-column ones would leave no TMEM for scales
-  static constexpr int ACC_BUFS = SCALED ? 1 : 2;
+  // two accumulators where they fit beside the ring's scale cells in the 512
+  // TMEM columns (a 256x192 scaled tile: 384 + 5 x 24); one for 256-wide scaled
+  // tiles, whose two accumulators would leave no column for the scales
+  static constexpr int ACC_BUFS = (!SCALED || 2 * BN + STAGES * SF_COLS_STAGE <= 512) ? 2 : 1;
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;
   static constexpr int MMA_K_BYTES = 32;
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;
@@ -1048,19 +1057,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(mapa_shared(&bars->acc_empty[buf], 0));
       };
       unsigned char* epi = C::EPI_TMA ? smem + C::EPI_OFF + q * C::EPI_BUFS * 4096 : nullptr;
+      // a half tile drains BN/64 chunks (only tiles that split have a half-tile path)
+      bool halved = false;
+      if constexpr (C::HALVES) {
+        if (half >= 0) {
+          halved = true;
+          if (C::EPI_TMA && p.y_tma)
+            drain_quadrant_tma<BN / 64, (C::EPI_BUFS > 0 ? C::EPI_BUFS : 1)>(taddr, col0, row - lane, p, release,
+                                                                             epi, &pm, nst);
+          else
+            drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
+        }
+      }
+      if (halved) continue;
       if constexpr (C::EPI_TMA) {
         if (p.y_tma) {
-          if (C::HALVES && half >= 0)
-            drain_quadrant_tma<BN / 64, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &pm, nst);
-          else
-            drain_quadrant_tma<BN / 32, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &pm, nst);
+          drain_quadrant_tma<BN / 32, C::EPI_BUFS>(taddr, col0, row - lane, p, release, epi, &pm, nst);
           continue;
         }
       }
-      if (C::HALVES && half >= 0)
-        drain_quadrant<BN / 64>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
-      else
-        drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
+      drain_quadrant<BN / 32>(taddr, yrow, col0, p.M, row_ok, p.col_exp, p, row - lane, release, epi, &pm);
     }
     // TMA stores still in flight complete before the CTA ends
     if (C::EPI_TMA && (p.npeers || p.y_tma) && lane == 0) bulk_wait_all();
@@ -1791,8 +1807,15 @@ cudaError_t launch_widen(const RunArgs& a) {
 }  // namespace
 
 bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
-  if (bn != 128 && bn != 256) return false;
   if (N <= 0 || K <= 0 || M <= 0) return false;
+  if (bn == 192) {   // CTA pairs, 256x192: the block-scaled kinds (two accumulators)
+    if (bm != 256) return false;
+    if (dt == kMX4X4) return K % 32 == 0;
+    if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;
+    if (dt == kMX8X4 || dt == kF8X4) return K % 128 == 0;
+    return false;
+  }
+  if (bn != 128 && bn != 256) return false;
   if (bm == 256) {   // CTA-pair tiles: the unscaled kinds, 256-wide
     if (bn != 256) return false;
     if (dt == kFP16) return K % 8 == 0 && M % 8 == 0;
@@ -1829,6 +1852,7 @@ size_t round256(size_t x) { return (x + 255) / 256 * 256; }
 struct ScaledWs {
   size_t a_bytes = 0, b_bytes = 0, wt_bytes = 0;
   int stages = 0, a_tiles = 0, b_tiles = 0, nb = 0, cells = 0;
+  int b_tile_rows = 0, b_chunks = 0;   // W rows per MMA tile (BN) and its 128-row chunks
   size_t total() const { return round256(a_bytes) + round256(b_bytes) + round256(wt_bytes); }
 };
 
@@ -1840,7 +1864,9 @@ ScaledWs scaled_ws(int dt, int bn, int N, int K, int M) {
   w.cells = w.nb / 4;   // 32-bit cells of 4 k-blocks per stage
   w.stages = (K + kps - 1) / kps;
   w.a_tiles = (N + 127) / 128;
-  w.b_tiles = (M + bn - 1) / bn * (bn / 128);
+  w.b_tile_rows = bn;
+  w.b_chunks = (bn + 127) / 128;
+  w.b_tiles = (M + bn - 1) / bn * w.b_chunks;
   const bool xp = (dt == kMX4X4 || dt == kMX8X4), wp = (dt != kF4F4);
   if (xp) w.a_bytes = (size_t)w.a_tiles * w.stages * w.cells * kSfChunk;
   if (wp) w.b_bytes = (size_t)w.b_tiles * w.stages * w.cells * kSfChunk;
@@ -1860,8 +1886,8 @@ cudaError_t launch_scaled(const RunArgs& a) {
   uint8_t* wt = base + round256(w.a_bytes) + round256(w.b_bytes);
   cudaError_t e;
   if (pa || pb) {
-    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles};
-    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles};
+    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles, 128, 1};
+    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles, w.b_tile_rows, w.b_chunks};
     const int tiles = w.a_tiles > w.b_tiles ? w.a_tiles : w.b_tiles;
     const int threads = tiles * w.stages * w.cells * 32;
     sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.cells);
@@ -1880,31 +1906,32 @@ cudaError_t launch_scaled(const RunArgs& a) {
 // Block-scaled kinds on CTA pairs (256x256 tiles): pack the scale planes into
 // per-stage blocks (one 512-byte block per 128 rows and cell), then the pair
 // kernel; each CTA brings its own rows' X scales and all 256 columns' W scales.
-template <int DT>
+template <int DT, int BN>
 cudaError_t launch_scaled_pair(const RunArgs& a) {
   constexpr int kStagesPair = 5;   // 5 x 35 KB leaves room for the TMA-store staging buffers
-  const ScaledWs w = scaled_ws(DT, 256, a.N, a.K, a.M);
+  const ScaledWs w = scaled_ws(DT, BN, a.N, a.K, a.M);
   if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
   uint8_t* base = static_cast<uint8_t*>(a.ws);
   uint8_t* pa = w.a_bytes ? base : nullptr;
   uint8_t* pb = w.b_bytes ? base + round256(w.a_bytes) : nullptr;
   if (pa || pb) {
-    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles};
-    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles};
+    SfPackJob ja{pa ? a.xscale : nullptr, pa, a.N, w.a_tiles, 128, 1};
+    SfPackJob jb{pb ? a.wscale : nullptr, pb, a.M, w.b_tiles, w.b_tile_rows, w.b_chunks};
     const int tiles = w.a_tiles > w.b_tiles ? w.a_tiles : w.b_tiles;
     const int threads = tiles * w.stages * w.cells * 32;
     sf_pack_kernel<<<dim3((threads + 255) / 256, 2), 256, 0, a.stream>>>(ja, jb, a.K / 32, w.stages, w.nb, w.cells);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  return launch_pair<DT, 256, kStagesPair>(a, a.W, pa, pb, w.a_tiles * w.stages * w.cells,
-                                           w.b_tiles * w.stages * w.cells);
+  return launch_pair<DT, BN, kStagesPair>(a, a.W, pa, pb, w.a_tiles * w.stages * w.cells,
+                                          w.b_tiles * w.stages * w.cells);
 }
 
 // f4f4 on CTA pairs: transpose W to [M,K] into the workspace (the 4-bit MMA
 // operands are K-major), then kind::mxf4 (E2M1 x E2M1) with unit scales.
+template <int BN>
 cudaError_t launch_f4f4_pair(const RunArgs& a) {
-  const ScaledWs w = scaled_ws(kF4F4, 256, a.N, a.K, a.M);
+  const ScaledWs w = scaled_ws(kF4F4, BN, a.N, a.K, a.M);
   if (!a.ws || a.ws_bytes < w.total() || !aligned(a.ws, 256)) return cudaErrorInvalidValue;
   uint8_t* wt = static_cast<uint8_t*>(a.ws) + round256(w.a_bytes) + round256(w.b_bytes);
   dim3 grid((a.M + kTrM - 1) / kTrM, (a.K + kTrK - 1) / kTrK);
@@ -1913,7 +1940,7 @@ cudaError_t launch_f4f4_pair(const RunArgs& a) {
   if (e != cudaSuccess) return e;
   // kind::mxf4 with unit scales (no scale planes: the kernel's block of UE8M0
   // 127s), on packed E2M1 straight from shared memory
-  return launch_pair<kF4F4, 256, 5>(a, wt);
+  return launch_pair<kF4F4, BN, 5>(a, wt);
 }
 
 }  // namespace
@@ -1978,6 +2005,15 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
   for (int i = 0; i < a.npeers; ++i)
     if (!a.ypeers || !aligned(a.ypeers[i], 16)) return cudaErrorInvalidValue;
   if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
+  if (bm == 256 && bn == 192) {   // block-scaled kinds, two accumulators
+    switch (a.dt) {
+      case kF4F4: return launch_f4f4_pair<192>(a);
+      case kMX4X4: return launch_scaled_pair<kMX4X4, 192>(a);
+      case kMX8X4: return launch_scaled_pair<kMX8X4, 192>(a);
+      case kF8X4: return launch_scaled_pair<kF8X4, 192>(a);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (bm == 256) {
     switch (a.dt) {
       case kFP16: return launch_pair<kFP16, 256, 6>(a, a.W);
@@ -1986,10 +2022,10 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
       case kINT8: return launch_widened_pair<kINT8>(a);
       case kFP8: return launch_widened_pair<kFP8>(a);
       case kMXFP4: return launch_widened_mx_pair(a);
-      case kF4F4: return launch_f4f4_pair(a);
-      case kMX4X4: return launch_scaled_pair<kMX4X4>(a);
-      case kMX8X4: return launch_scaled_pair<kMX8X4>(a);
-      case kF8X4: return launch_scaled_pair<kF8X4>(a);
+      case kF4F4: return launch_f4f4_pair<256>(a);
+      case kMX4X4: return launch_scaled_pair<kMX4X4, 256>(a);
+      case kMX8X4: return launch_scaled_pair<kMX8X4, 256>(a);
+      case kF8X4: return launch_scaled_pair<kF8X4, 256>(a);
       default: return cudaErrorInvalidValue;
     }
   }

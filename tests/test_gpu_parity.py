@@ -61,8 +61,9 @@ def assert_close(dtype, out, ref):
 TC_TILES = {d: ["256x256", "128x256", "128x128"] for d in ("fp16", "i8i8", "f8f8")}
 TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("int8", "fp8")})   # 256x256: W widened once
 TC_TILES.update({"mxfp4": ["256x256", "128x256", "128x128"]})   # 256x256: widened once to f16 [K,M]
-TC_TILES.update({"f4f4": ["256x256", "128x256", "128x128"]})
-TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
+# block-scaled kinds (and f4f4 on kind::mxf4) also run 256x192 CTA pairs with two accumulators
+TC_TILES.update({"f4f4": ["256x256", "256x192", "128x256", "128x128"]})
+TC_TILES.update({d: ["256x256", "256x192", "128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
 TC_CASES = [(d, t) for d in F.DTYPES for t in TC_TILES[d]]
 
 
