@@ -538,7 +538,15 @@ int gemm_time_e2e_pipelined(int device, int dtype, int tile, const void* hX, voi
   if (!ok) rc = cuda_fail(cudaGetLastError(), "pipeline streams / events");
   for (int i = 0; i < warmup + iters && rc == GEMM_OK; ++i) {
     const int b = i & 1;
-    if (i == warmup) cudaEventRecord(t0, sin);
+    if (i == warmup) {
+      // the warm-up steps' copies out may still be running on `sout`: drain all
+      // three streams first, so that the timed window holds the timed steps only
+      // (and the fill of the first one)
+      cudaStreamSynchronize(sin);
+      cudaStreamSynchronize(st);
+      cudaStreamSynchronize(sout);
+      cudaEventRecord(t0, sin);
+    }
     cudaStreamWaitEvent(sin, gemm_done[b], 0);   // step i-2 has consumed this X set
     cudaMemcpyAsync(dX[b], hX, xb, cudaMemcpyHostToDevice, sin);
     if (xsb) cudaMemcpyAsync(dXS[b], hxscale, xsb, cudaMemcpyHostToDevice, sin);

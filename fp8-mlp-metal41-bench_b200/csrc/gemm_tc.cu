@@ -500,17 +500,28 @@ __device__ __forceinline__ void drain_quadrant_tma(uint32_t taddr0, int col0, in
     }
     ++nst;
   };
-  uint32_t ra[32], rb[32];
-  tmem_ld_32x32b_x32(taddr0, ra);
+  // TMEM loads in groups of two chunks (two 32-column loads in flight per wait),
+  // double-buffered: group g + 1 loads while group g is staged and stored
+  constexpr int NG = NCH / 2;
+  uint32_t ra0[32], ra1[32], rb0[32], rb1[32];
+  auto load_group = [&](int g, uint32_t (&x0)[32], uint32_t (&x1)[32]) {
+    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((2 * g) * 32), x0);
+    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((2 * g + 1) * 32), x1);
+  };
+  load_group(0, ra0, ra1);
 #pragma unroll 1
-  for (int c = 0; c < NCH; c += 2) {
-    tmem_ld_wait();                                            // chunk c in ra
-    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 1) * 32), rb);
-    put(ra, c);
-    tmem_ld_wait();                                            // chunk c + 1 in rb
-    if (c + 2 < NCH) tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 2) * 32), ra);
+  for (int g = 0; g < NG; g += 2) {
+    tmem_ld_wait();                                            // group g in ra
+    if (g + 1 < NG) load_group(g + 1, rb0, rb1);
     else release();
-    put(rb, c + 1);
+    put(ra0, 2 * g);
+    put(ra1, 2 * g + 1);
+    if (g + 1 >= NG) break;
+    tmem_ld_wait();                                            // group g + 1 in rb
+    if (g + 2 < NG) load_group(g + 2, ra0, ra1);
+    else release();
+    put(rb0, 2 * g + 2);
+    put(rb1, 2 * g + 3);
   }
 }
 

@@ -198,8 +198,9 @@ int gemm_time_e2e(int device, int dtype, int tile, const void *hX, void *dX,
  * two device sets of X / Y are used in turn, so that step i's Y copy overlaps
  * step i+1's X copy and GEMM (the two copy directions run on separate engines).
  * Every step still moves its own inputs in and its own result out.  After
- * `warmup` untimed steps, *total_ms receives the time of `iters` steps, from the
- * first timed copy in to the last copy out.  The serving-loop form of runOnce
+ * `warmup` untimed steps (and once their last copy out has finished), *total_ms
+ * receives the time of `iters` steps, from the first timed copy in to the last
+ * copy out.  The serving-loop form of runOnce
  * (main.swift:486-518) with the host copies that a plugin host adds. */
 int gemm_time_e2e_pipelined(int device, int dtype, int tile, const void *hX, void *dX0, void *dX1,
                             const void *dW, void *dY0, void *dY1, void *hY, int N, int K, int M,
