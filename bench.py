@@ -436,6 +436,7 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
     rows = []
     windows = []
     shared_w = {}
+    read_ceiling = {}   # bytes -> median ms of a plain streaming read of that many bytes
     for sname, N, K, M, iters in SUITE:
         ops = Operands(N, K, M, "seeded", 0)
         # the thin and fat rows share K and M, hence the very same seeded W planes
@@ -476,9 +477,22 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
                    "value": flops / (med / 1e3) / 1e12, "unit": unit_of(dtype),
                    "parity_ok": ok, "max_rel": rel, "clocks": w.summary()}
             if N <= 16:
-                gbs = F.algorithmic_bytes(dtype, N, K, M) / (med / 1e3) / 1e9
+                nb = F.algorithmic_bytes(dtype, N, K, M)
+                gbs = nb / (med / 1e3) / 1e9
+                nb16 = (nb + 15) // 16 * 16
+                if nb16 not in read_ceiling:
+                    rbuf = d.zeros(nb16)
+                    read_ceiling[nb16] = statistics.median(
+                        G.read_probe(0, rbuf, nb16, warmup=3, iters=iters, flush=FL, flush_bytes=FLUSH_BYTES))
+                    del rbuf
+                rms = read_ceiling[nb16]
                 row.update({"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / hbm,
-                            "peak": hbm, "peak_source": f"{src} hbm_gbs"})
+                            "peak": hbm, "peak_source": f"{src} hbm_gbs",
+                            "read_ceiling": {"bytes": nb16, "ms_median": rms, "gbs": nb16 / (rms / 1e3) / 1e9,
+                                             "frac": nb16 / (rms / 1e3) / 1e9 / hbm,
+                                             "what": "gemm_read_probe: plain 16-byte streaming read of the "
+                                                     "same byte count, cold L2"},
+                            "of_read_ceiling": rms / med})
             else:
                 peak = bf16 * KIND_RATIO[kind]
                 pp = probe.get(kind_probe)

@@ -42,6 +42,14 @@ bool stream_supported(int dt, int N, int K, int M);
 size_t stream_workspace(int dt, int N, int K, int M);
 cudaError_t launch_stream(const RunArgs& a);
 
+// ---- thin rows on the warp-level tensor-core MMA (gemv_mma.cu, tile "gemv.mma") --
+// N <= 16 for fp16, int8, fp8, f8f8 ([K,M]) and the four MX kinds ([M,K]):
+// persistent stream-K over slabs of the weights, mma.sync.m16n8k16 on weights
+// widened to f16 in registers.  The workspace holds slab counters and partials.
+bool mma_supported(int dt, int N, int K, int M);
+size_t mma_workspace(int dt, int N, int K, int M);
+cudaError_t launch_mma(const RunArgs& a);
+
 // ---- thin rows on the tensor cores (N <= 16; weights as the MMA's A operand) ----
 // Stream-K over (128-row weight tile, K stage) units, one CTA per SM; shared
 // tiles are summed through the workspace (counters zero before first use).
@@ -63,6 +71,11 @@ bool tc_gather_supported(int dt, int bm);
 // lines of it afterwards: a cold cache for the next kernel, without the dirty
 // write-back a memset would leave behind (defined in gemv.cu).
 cudaError_t launch_l2_flush(const void* buf, size_t bytes, int num_sms, cudaStream_t st);
+
+// One read of `bytes` (a multiple of 16, 16-byte aligned) of `buf` with 16-byte
+// streaming loads and nothing else: the HBM read ceiling the GEMVs are held to
+// (defined in gemv.cu).
+cudaError_t launch_read_probe(const void* buf, size_t bytes, int num_sms, cudaStream_t st);
 
 // Record a message for gemm_last_error() (defined in api.cu).
 void set_last_error(const char* msg);

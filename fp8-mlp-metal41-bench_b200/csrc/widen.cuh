@@ -60,6 +60,18 @@ __device__ __forceinline__ uint4 widen_e4m3x8(uint2 v) {
   return o;
 }
 
+// 8 E2M1 (one word, low nibble first) -> 4 f16 pairs, unscaled (exact).
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
 // 8 E2M1 (one word, low nibble first) -> 8 f16, times the f16x2 multiplier.
 __device__ __forceinline__ uint4 widen_e2m1x8(uint32_t w, uint32_t mul) {
   uint32_t h0, h1, h2, h3;

@@ -23,6 +23,7 @@ EXPORTS = [
     "gemm_workspace_size", "gemm_alloc", "gemm_free", "gemm_memset", "gemm_h2d", "gemm_d2h",
     "gemm_host_alloc", "gemm_host_free", "gemm_run", "gemm_sync", "gemm_time",
     "gemm_time_e2e", "gemm_time_e2e_pipelined", "gemm_launches_per_run", "gemm_peak_probe",
+    "gemm_read_probe",
     "gemm_run_noalloc",
     "gemm_quantize",
     "gemm_run_gather", "gemm_gather_supported", "gemm_peer_alloc", "gemm_peer_open", "gemm_peer_close",
@@ -90,6 +91,8 @@ def _declare(L):
                                             ctypes.POINTER(ctypes.c_float)]),
         "gemm_launches_per_run": (c_int, [c_int, c_int, c_int, c_int, c_int]),
         "gemm_peak_probe": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(ctypes.c_double)]),
+        "gemm_read_probe": (c_int, [c_int, vp, c_size, c_int, c_int, vp, c_size,
+                                    ctypes.POINTER(ctypes.c_float)]),
         "gemm_run_noalloc": (c_int, [c_int, c_int, c_int, vp, vp, vp, c_int, c_int, c_int, vp, vp,
                                      vp]),
         "gemm_quantize": (c_int, [c_int, c_int, vp, vp, vp, ctypes.c_long, ctypes.c_long, vp]),
@@ -340,6 +343,15 @@ def peak_probe(device: int, kind: int, reps: int = 4096, iters: int = 10) -> flo
     v = ctypes.c_double(0.0)
     check(lib().gemm_peak_probe(device, kind, reps, iters, ctypes.byref(v)), "gemm_peak_probe")
     return v.value
+
+
+def read_probe(device: int, buf, nbytes: int, warmup: int = 3, iters: int = 20, flush=None,
+               flush_bytes: int = 0) -> list:
+    """CUDA-event times (ms) of a plain streaming read of `nbytes` of `buf`."""
+    out = (ctypes.c_float * iters)()
+    check(lib().gemm_read_probe(device, as_ptr(buf), int(nbytes), warmup, iters, as_ptr(flush),
+                                int(flush_bytes), out), "gemm_read_probe")
+    return list(out)
 
 
 def quantize(device, fmt, src, dst, scales=None, rows=1, cols=1, stream=None) -> None:

@@ -92,7 +92,10 @@ const char *gemm_kernel_name(int dtype);
 /* The tile list that replaces the reference's ten BMxBN threadgroup tiles
  * (main.swift:135-143, fp8_mlp.metal:446-450).  Tensor-core tiles are named
  * "<BM>x<BN>" (BM rows of Y per CTA, BN columns); the CUDA-core split-K
- * kernels for thin rows are named "gemv.k<S>" (S = K splits). */
+ * kernels for thin rows are named "gemv.k<S>" (S = K splits); "16x128" is the
+ * tcgen05 thin tile, "stream" the persistent streaming GEMV and "gemv.mma" the
+ * thin tile on warp-level MMAs (N <= 16; fp16, int8, fp8, f8f8 with K % 4 and
+ * 16-byte weight rows, the MX kinds with K % 128). */
 int gemm_num_tiles(void);
 const char *gemm_tile_name(int tile);
 int gemm_tile_index(const char *name);          /* -1 if unknown */
@@ -243,6 +246,18 @@ int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const voi
  * reports the median dense TFLOP/s (TOP/s for i8).  The probe allocates a
  * few hundred bytes of device memory for its result sink. */
 int gemm_peak_probe(int device, int kind, int reps, int iters, double *tflops_out);
+
+/* Plain streaming read of `bytes` (a non-zero multiple of 16) of the device
+ * buffer `buf` (16-byte aligned): coalesced 16-byte loads, eight in flight per
+ * thread, one 32 KB run per 256-thread CTA, nothing decoded or written.  The
+ * reference has no counterpart; it is the practical HBM ceiling that the
+ * thin-row (N <= 16, main.swift:146-150) GEMVs are reported against.  Runs
+ * `warmup` untimed launches, then `iters` timed ones on the device's library
+ * stream, each preceded (when flush/flush_bytes are given) by a read of the
+ * flush buffer so that L2 holds none of `buf`; writes one CUDA-event time (ms)
+ * per timed launch to ms_out[0..iters). */
+int gemm_read_probe(int device, const void *buf, size_t bytes, int warmup, int iters, void *flush,
+                    size_t flush_bytes, float *ms_out);
 
 /* ---- quantisers: the operand formats produced from f32 on the device ---------
  * Replaces the reference's host-side producers, which run untimed before the

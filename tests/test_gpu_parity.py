@@ -416,3 +416,75 @@ def test_gather_rejects_unsupported_tiles(gemm):
     with pytest.raises(G.GemmError) as e:
         G.run_gather(0, dt, G.tile_index("256x256"), X2, W2, Y2, N, K, M, None, None, None, 0, peers=[P2] * 8)
     assert e.value.code == 1 and "npeers" in str(e.value)
+
+
+# thin rows on the warp-level tensor-core MMA (tile gemv.mma): stream-K over
+# weight slabs, mma.sync on weights widened to f16 in registers
+MMA_DT = ["fp16", "int8", "fp8", "f8f8", "mxfp4", "mxfp4/a4", "mxfp4/a8", "mxfp4/f8"]
+
+
+def mma_shape(dtype, N, K, M):
+    # [K,M] weights: K % 4 and 16-byte rows; MX weights: K % 128 (steps of 4 blocks)
+    if dtype in F.W_MX:
+        return N, max(128, K // 128 * 128), M
+    return N, max(4, K // 4 * 4), (M // 16 * 16 or 16)
+
+
+@pytest.mark.parametrize("dtype", MMA_DT)
+@pytest.mark.parametrize("shape", [(1, 4096, 11008), (1, 1024, 1504), (3, 1000, 1296), (8, 512, 1040),
+                                   (16, 512, 640), (5, 64, 128), (2, 8192, 256), (7, 200, 4096),
+                                   (1, 36, 50), (12, 4096, 300)])
+def test_mma_thin_rows(gemm, dtype, shape):
+    # whole slabs, slabs shared by many CTAs (K=8192, few slabs), a single
+    # step, ragged K and ragged M (a part-filled last slab), N > 8 (row blocks)
+    N, K, M = mma_shape(dtype, *shape)
+    out, ref, _ = run_case(gemm, dtype, "gemv.mma", N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", MMA_DT)
+def test_mma_thin_reference_patterns(gemm, dtype):
+    out, ref, _ = run_case(gemm, dtype, "gemv.mma", 4, 1024, 768, mode="ref")
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("lo,hi", [(124, 130), (90, 100), (40, 214)])
+def test_mma_mxfp4_any_scale_range(gemm, lo, hi):
+    # each 32-element block is folded into f32 times its own 2^(s - 127): no
+    # range limit, the whole output stays within the tolerance
+    N, K, M = 3, 2048, 384
+    ops = Operands(N, K, M, "seeded", 4)
+    rng = np.random.default_rng(11)
+    ops._cache["wscale"] = rng.integers(lo, hi + 1, M * (K // 32), dtype=np.uint8)
+    out, ref, _ = run_case(gemm, "mxfp4", "gemv.mma", N, K, M, ops=ops)
+    assert_close("mxfp4", out, ref)
+
+
+@pytest.mark.parametrize("dtype", ["int8", "mxfp4/a8"])
+def test_mma_thin_deterministic(gemm, dtype):
+    # two calls on ONE workspace: identical bits (slabs summed in CTA order)
+    # and the slab counters are back at zero for the second call
+    a, ref, ops = run_case(gemm, dtype, "gemv.mma", 2, 4096, 11008)
+    b, _, _ = run_case(gemm, dtype, "gemv.mma", 2, 4096, 11008, ops=ops)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert_close(dtype, a, ref)
+
+
+def test_mma_rejects_unsupported(gemm):
+    G = gemm
+    ti = G.tile_index("gemv.mma")
+    assert not G.tile_supported(F.CODE["i8i8"], ti, 1, 4096, 11008)
+    assert not G.tile_supported(F.CODE["int8"], ti, 1, 4096, 11000)   # rows not whole 16-byte chunks
+    assert not G.tile_supported(F.CODE["fp8"], ti, 17, 4096, 11008)   # N > 16
+
+
+@pytest.mark.parametrize("dtype", ["mxfp4/a4", "mxfp4/a8", "mxfp4/f8"])
+@pytest.mark.parametrize("N", [3, 8, 16])
+def test_default_tile_mx_quantized_x(gemm, dtype, N):
+    # the default tile of the MX kinds with E2M1 / E4M3 activations at
+    # 3 <= N <= 16 is the warp-MMA thin tile; it matches the oracle there
+    K, M = 4096, 1040
+    ti = gemm.default_tile(F.CODE[dtype], N, K, M)
+    assert gemm.tile_names()[ti] == "gemv.mma"
+    out, ref, _ = run_case(gemm, dtype, "gemv.mma", N, K, M)
+    assert_close(dtype, out, ref)

@@ -56,6 +56,24 @@ def test_peak_probe_rejects_unknown_kind(gemm):
     assert e.value.code == gemm.GEMM_ERR_ARGS
 
 
+def test_read_probe_rate_and_arguments(gemm):
+    """The streaming-read ceiling of the thin rows: a 64 MiB read from a cold L2
+    must land between a fifth of B200's nominal 7.7 TB/s and just above it, and
+    a misaligned or ragged request is an argument error."""
+    import torch
+    nb = 64 << 20
+    buf = torch.zeros(nb, dtype=torch.uint8, device="cuda:0")
+    fl = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda:0")
+    ms = gemm.read_probe(0, buf, nb, warmup=2, iters=5, flush=fl, flush_bytes=fl.numel())
+    gbs = nb / (sorted(ms)[len(ms) // 2] / 1e3) / 1e9
+    print(f"read probe: {gbs:.0f} GB/s")
+    assert math.isfinite(gbs) and 0.2 * 7700 < gbs < 1.1 * 7700
+    for args in ((buf, nb - 8), (buf[1:], 1 << 20), (buf, 0)):
+        with pytest.raises(gemm.GemmError) as e:
+            gemm.read_probe(0, args[0], args[1], warmup=0, iters=1)
+        assert e.value.code == gemm.GEMM_ERR_ARGS
+
+
 @pytest.mark.parametrize("dtype,N,K,M", [("i8i8", 256, 512, 768), ("mxfp4", 1, 1024, 1536),
                                          ("mxfp4/a8", 384, 512, 640)])
 def test_autotune_writes_a_profile_and_picks_a_parity_green_tile(gemm, tmp_path, monkeypatch, capsys, dtype,
