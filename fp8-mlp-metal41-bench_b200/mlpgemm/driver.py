@@ -12,7 +12,9 @@ Added flags (all optional): --gpus 1|2|4|8 (sharded across GPUs; run
 under torchrun), --shard m|n (split W's columns, the default, or X's rows),
 --allgather (gather Y over NCCL, timed separately),
 --data ref|seeded, --seed S, --rotate R (R weight copies used round-robin),
---flush (overwrite a >L2 buffer before every timed iteration).
+--flush (overwrite a >L2 buffer before every timed iteration),
+--read-probe BYTES (time a plain streaming read of BYTES from a cold L2,
+the practical ceiling of the HBM-bound thin rows, instead of the GEMM).
 """
 from __future__ import annotations
 
@@ -43,6 +45,7 @@ SUITE = [ShapeCase("square", 4096, 4096, 4096, 100), ShapeCase("thin", 1, 4096, 
          ShapeCase("fat", 2048, 4096, 11008, 50)]
 
 BOOL_FLAGS = ("--suite", "--autotune", "--no-profile", "--allgather", "--flush", "--peak")
+FLUSH_BYTES = 256 << 20   # read before each timed launch with --flush: larger than the 126 MB L2
 
 
 @dataclass
@@ -66,6 +69,7 @@ class Args:
     rotate: int = 1
     flush: bool = False
     peak: bool = False      # tensor-core peak probe instead of the GEMM (tune/peak.swift)
+    read_bytes: int = 0     # > 0: streaming-read probe of that many bytes instead of the GEMM
 
 
 class BenchExit(Exception):
@@ -151,6 +155,8 @@ def parse_args(argv, tiles=None) -> Args:
             a.seed = val
         elif key == "--rotate":
             a.rotate = max(1, val)
+        elif key == "--read-probe":
+            a.read_bytes = max(0, val)
         i += 1
     return a
 
@@ -334,11 +340,11 @@ def run_dtype(rn: Runner, dtype: str, tile: str, N, K, M, warmup, iters, W=None,
     Y = rn.scratch(("Y", N, M), N * M * 4)
     wsb = G.workspace_size(dt, ti, N, K, M)
     WSP = rn.scratch(("ws", wsb), wsb) if wsb else None
-    fl = rn.scratch("flush", 256 << 20) if flush else None
+    fl = rn.scratch("flush", FLUSH_BYTES) if flush else None
     Y.zero()
     ms = G.time(rn.device, dt, ti, X, Ws, Y, N, K, M, xscale=XS, wscales=WS, workspace=WSP,
                 workspace_bytes=wsb, warmup=warmup, iters=iters, flush=fl,
-                flush_bytes=(256 << 20) if flush else 0)
+                flush_bytes=FLUSH_BYTES if flush else 0)
     host = np.empty((N, M), dtype=np.int32 if dtype == "i8i8" else np.float32)
     Y.download(host)
     return ms, host
@@ -451,6 +457,26 @@ def run_peak(a) -> int:
     return 0
 
 
+def run_read_probe(a) -> int:
+    """A plain streaming read of --read-probe bytes (rounded up to 16), each
+    timed launch after a 256 MiB L2 flush: the practical HBM ceiling that the
+    thin rows (N <= 16, main.swift:146-150) are reported against.  --iters sets
+    the timed launches (default 100), --warmup the untimed ones."""
+    if G.device_count() < 1:
+        raise BenchExit(1, "No CUDA device")
+    G.init(0)
+    nb = (a.read_bytes + 15) // 16 * 16
+    iters = a.iters if a.shape_set else 100
+    buf = G.DeviceBuffer(0, nb).zero()
+    flush = G.DeviceBuffer(0, FLUSH_BYTES).zero()
+    ms = G.read_probe(0, buf, nb, warmup=max(a.warmup, 1), iters=iters, flush=flush, flush_bytes=FLUSH_BYTES)
+    med, mean = float(np.median(ms)), float(np.mean(ms))
+    print(f"read probe: {nb} bytes, cold L2, {iters} launches")
+    print(f"median {med * 1e3:.2f} us  mean {mean * 1e3:.2f} us  {nb / (mean * 1e-3) / 1e9:.0f} GB/s (mean)")
+    sys.stdout.flush()
+    return 0
+
+
 def _main(argv) -> int:
     try:
         tiles = G.tile_names()
@@ -459,6 +485,8 @@ def _main(argv) -> int:
     a = parse_args(argv, tiles)
     if a.peak:
         return run_peak(a)
+    if a.read_bytes > 0:
+        return run_read_probe(a)
     shapes = shapes_for(a)
     for s in shapes:
         if s.N <= 0 or s.K <= 0 or s.M <= 0 or s.iters <= 0:

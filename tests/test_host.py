@@ -93,6 +93,9 @@ def test_parse_args_quirks():
     assert e.value.code == 1 and "Unknown --tile 64x32" in e.value.msg
     a = D.parse_args(["--peak", "--iters", "3"], tiles)     # peak probe mode (tune/peak.swift)
     assert a.peak and a.iters == 3 and not a.suite
+    a = D.parse_args(["--read-probe", "45133824"], tiles)   # streaming-read ceiling instead of the GEMM
+    assert a.read_bytes == 45133824 and not a.shape_set
+    assert D.parse_args(["--read-probe", "-5"], tiles).read_bytes == 0 == D.parse_args([], tiles).read_bytes
     a = D.parse_args(["--gpus", "2", "--shard", "N", "--allgather"], tiles)
     assert a.gpus == 2 and a.shard == "n" and a.allgather
     assert D.parse_args([], tiles).shard == "m"
