@@ -216,6 +216,7 @@ struct Bars {
   uint64_t acc_empty[2];
   uint32_t tmem_base;
   int abort_flag;
+  uint64_t sf_ready[8];   // block-scaled kinds: a stage's scale cells are in TMEM
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int& tn) {
@@ -550,6 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->acc_full[b], 1);
       mbar_init(&bars->acc_empty[b], 4 * 32);
     }
+    if constexpr (C::SCALED)
+      for (int st = 0; st < STAGES; ++st) mbar_init(&bars->sf_ready[st], 1);
     bars->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -627,21 +630,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (!mbar_try_wait(a, filled_parity[s]) && global_ns() - t0 < kWaitTimeoutNs) {}
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------ MMA issuer --------------------------------
+  } else if (C::SCALED && warp == 3 && lane == 0) {
+    // --------------------- scale-cell copier (block-scaled kinds) ---------------
+    // A stage's scale blocks go to TMEM with tcgen05.cp from this thread, which
+    // commits them to the stage's sf_ready barrier; the MMA issuer waits on that
+    // barrier in place of `full`.  With the copies in the MMA thread's own loop
+    // (right before each stage's MMAs) the block-scaled tiles measured 7-14 %
+    // slower: that single thread paces these kernels.
     uint32_t stage = 0, phase = 0;
-    int local = 0;
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
-    // Block-scaled kinds: the scale blocks of a stage go to TMEM with tcgen05.cp
-    // right before that stage's MMAs.  (Copying the next stage's blocks ahead of
-    // the current stage's MMAs measured 5-9 % slower: the copies sit in the same
-    // in-order tensor pipe.)
-    auto copy_sf = [&](uint32_t stg) {
-      if constexpr (C::SCALED) {
-        const uint32_t sf_smem = smem_base + C::SF_OFF + stg * C::SF_STAGE_BYTES;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x500 + stage)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
         const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
-        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stg * C::SF_COLS_STAGE);
+        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
           const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
@@ -652,8 +657,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
                                                    : sf_const, 0, 128));
         }
+        tc_commit(&bars->sf_ready[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
-    };
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------ MMA issuer --------------------------------
+    uint32_t stage = 0, phase = 0;
+    int local = 0;
+    bool ok = true;
+    const uint32_t smem_base = smem_u32(smem);
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
@@ -661,13 +674,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * C::ACC_COLS);
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x300 + stage)) { ok = false; break; }
+        // block-scaled kinds: the copier has also put the stage's scale cells in TMEM
+        uint64_t* ready = C::SCALED ? &bars->sf_ready[stage] : &bars->full[stage];
+        if (!mbar_wait(ready, phase, ctl, 0x300 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
         const uint32_t b_addr = a_addr + C::A_BYTES;
         if constexpr (C::SCALED) {
           const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
-          copy_sf(stage);
 #pragma unroll
           for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
             constexpr int per_cell = 4 / T::nsf;   // MMAs served by one cell
@@ -896,6 +910,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->acc_full[b], 1);
       mbar_init(&bars->acc_empty[b], 2 * 4);            // one arrival per epilogue warp, both CTAs
     }
+    if constexpr (C::SCALED)
+      for (int st = 0; st < STAGES; ++st) mbar_init(&bars->sf_ready[st], 1);   // leader's copier
     bars->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -977,18 +993,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     aborted_any = !ok;
-  } else if (warp == 1 && lane == 0 && rank == 0) {
-    // ------------------------ MMA issuer (leader only) ------------------------
+  } else if (C::SCALED && warp == 3 && lane == 0 && rank == 0) {
+    // --------------- scale-cell copier (block-scaled kinds, leader only) ---------
+    // A stage's scale blocks go to both CTAs' TMEM with tcgen05.cp.cta_group::2
+    // from this thread, committed to the leader's sf_ready barrier, on which the
+    // MMA issuer waits in place of `full`.  Copying them in the MMA thread's own
+    // loop measured 7-14 % slower: that single thread paces the scaled tiles.
     uint32_t stage = 0, phase = 0;
-    int local = 0;
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
-    // scale blocks of a stage go to both CTAs' TMEM right before that stage's MMAs
-    auto copy_sf = [&](uint32_t stg) {
-      if constexpr (C::SCALED) {
-        const uint32_t sf_smem = smem_base + C::SF_OFF + stg * C::SF_STAGE_BYTES;
+    for (int item = pair; item < num_items && ok; item += npairs) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x500 + stage)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
         const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
-        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stg * C::SF_COLS_STAGE);
+        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
           const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
@@ -999,8 +1019,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
                                                         : sf_const, 0, 128));
         }
+        tc_commit_pair(&bars->sf_ready[stage], 0x1);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
-    };
+    }
+    aborted_any = !ok;
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------ MMA issuer (leader only) ------------------------
+    uint32_t stage = 0, phase = 0;
+    int local = 0;
+    bool ok = true;
+    const uint32_t smem_base = smem_u32(smem);
     for (int item = pair; item < num_items && ok; item += npairs, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
@@ -1009,13 +1038,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
       const uint32_t idesc = (C::HALVES && item >= p.split_from) ? C::IDESC_H : C::IDESC;   // N = BN/2 for a half
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&bars->full[stage], phase, ctl, 0x300 + stage)) { ok = false; break; }
+        // block-scaled kinds: the copier has also put the stage's scale cells in TMEM
+        uint64_t* ready = C::SCALED ? &bars->sf_ready[stage] : &bars->full[stage];
+        if (!mbar_wait(ready, phase, ctl, 0x300 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
         const uint32_t b_addr = a_addr + C::A_BYTES;
         if constexpr (C::SCALED) {
           const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
-          copy_sf(stage);
 #pragma unroll
           for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
             constexpr int per_cell = 4 / T::nsf;
