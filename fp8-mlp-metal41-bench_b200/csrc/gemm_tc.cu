@@ -637,25 +637,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // barrier in place of `full`.  With the copies in the MMA thread's own loop
     // (right before each stage's MMAs) the block-scaled tiles measured 7-14 %
     // slower: that single thread paces these kernels.
+    // (an operand without a scale plane has unit cells, which the MMA issuer
+    // copies into every slot once; with no plane at all this thread has no work)
     uint32_t stage = 0, phase = 0;
     bool ok = true;
+    const bool work = p.sfa || p.sfb;
     const uint32_t smem_base = smem_u32(smem);
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int tile = blockIdx.x; work && tile < num_tiles && ok; tile += gridDim.x) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&bars->full[stage], phase, ctl, 0x500 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
-        const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
         const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
           const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
-          tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + g * kSfChunk : sf_const, 0, 128));
+          if (p.sfa) tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(sf_smem + g * kSfChunk, 0, 128));
+          if (p.sfb) {
 #pragma unroll
-          for (int c = 0; c < C::SF_B_CHUNKS; ++c)
-            tc_cp_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
-                                 sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
-                                                   : sf_const, 0, 128));
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
+                                   sdesc_plain(sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk, 0, 128));
+          }
         }
         tc_commit(&bars->sf_ready[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -667,6 +670,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
+    if constexpr (C::SCALED) {
+      // unit scale cells (the block of 127s) for an operand without a scale
+      // plane go into every ring slot once; this thread's MMAs follow them in
+      // issue order
+      const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
+      for (int st = 0; st < STAGES; ++st) {
+        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + st * C::SF_COLS_STAGE);
+#pragma unroll
+        for (int g = 0; g < C::SF_CELLS; ++g) {
+          const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+          if (!p.sfa) tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(sf_const, 0, 128));
+          if (!p.sfb) {
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c, sdesc_plain(sf_const, 0, 128));
+          }
+        }
+      }
+    }
+    const bool via_copier = C::SCALED && (p.sfa || p.sfb);
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
@@ -675,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t d_tmem = tmem_base + (uint32_t)(buf * C::ACC_COLS);
       for (int kb = 0; kb < p.num_kb; ++kb) {
         // block-scaled kinds: the copier has also put the stage's scale cells in TMEM
-        uint64_t* ready = C::SCALED ? &bars->sf_ready[stage] : &bars->full[stage];
+        uint64_t* ready = via_copier ? &bars->sf_ready[stage] : &bars->full[stage];
         if (!mbar_wait(ready, phase, ctl, 0x300 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
@@ -999,25 +1022,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     // from this thread, committed to the leader's sf_ready barrier, on which the
     // MMA issuer waits in place of `full`.  Copying them in the MMA thread's own
     // loop measured 7-14 % slower: that single thread paces the scaled tiles.
+    // (an operand without a scale plane has unit cells, which the MMA issuer
+    // copies into every slot once; with no plane at all this thread has no work)
     uint32_t stage = 0, phase = 0;
     bool ok = true;
+    const bool work = p.sfa || p.sfb;
     const uint32_t smem_base = smem_u32(smem);
-    for (int item = pair; item < num_items && ok; item += npairs) {
+    for (int item = pair; work && item < num_items && ok; item += npairs) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&bars->full[stage], phase, ctl, 0x500 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
-        const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
         const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
           const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
-          tc_cp_pair_32x128b_warpx4(sfa_t, sdesc_plain(p.sfa ? sf_smem + g * kSfChunk : sf_const, 0, 128));
+          if (p.sfa) tc_cp_pair_32x128b_warpx4(sfa_t, sdesc_plain(sf_smem + g * kSfChunk, 0, 128));
+          if (p.sfb) {
 #pragma unroll
-          for (int c = 0; c < C::SF_B_CHUNKS; ++c)
-            tc_cp_pair_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
-                                      sdesc_plain(p.sfb ? sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk
-                                                        : sf_const, 0, 128));
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_pair_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c,
+                                        sdesc_plain(sf_smem + C::SF_A_BYTES + (c * C::SF_CELLS + g) * kSfChunk, 0,
+                                                    128));
+          }
         }
         tc_commit_pair(&bars->sf_ready[stage], 0x1);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -1030,6 +1057,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     bool ok = true;
     const uint32_t smem_base = smem_u32(smem);
+    if constexpr (C::SCALED) {
+      // unit scale cells (the block of 127s) for an operand without a scale
+      // plane go into every ring slot of both CTAs once; this thread's MMAs
+      // follow them in issue order
+      const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
+      for (int st = 0; st < STAGES; ++st) {
+        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + st * C::SF_COLS_STAGE);
+#pragma unroll
+        for (int g = 0; g < C::SF_CELLS; ++g) {
+          const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
+          if (!p.sfa) tc_cp_pair_32x128b_warpx4(sfa_t, sdesc_plain(sf_const, 0, 128));
+          if (!p.sfb) {
+#pragma unroll
+            for (int c = 0; c < C::SF_B_CHUNKS; ++c)
+              tc_cp_pair_32x128b_warpx4(sfa_t + C::SF_COLS_A + 4 * c, sdesc_plain(sf_const, 0, 128));
+          }
+        }
+      }
+    }
+    const bool via_copier = C::SCALED && (p.sfa || p.sfb);
     for (int item = pair; item < num_items && ok; item += npairs, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
@@ -1039,7 +1086,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = (C::HALVES && item >= p.split_from) ? C::IDESC_H : C::IDESC;   // N = BN/2 for a half
       for (int kb = 0; kb < p.num_kb; ++kb) {
         // block-scaled kinds: the copier has also put the stage's scale cells in TMEM
-        uint64_t* ready = C::SCALED ? &bars->sf_ready[stage] : &bars->full[stage];
+        uint64_t* ready = via_copier ? &bars->sf_ready[stage] : &bars->full[stage];
         if (!mbar_wait(ready, phase, ctl, 0x300 + stage)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
