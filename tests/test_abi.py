@@ -67,6 +67,12 @@ def test_layout_rules_and_tile_support():
     for d in ("fp16", "int8", "i8i8", "fp8", "f8f8", "mxfp4"):
         assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "16x128"
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 8, 4096, 11008)].startswith("gemv")
+    # MX kinds with E2M1 / E4M3 activations at 3 <= N <= 16: the warp-MMA thin tile
+    for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8"):
+        assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "gemv.mma"
+        assert G.tile_names()[G.default_tile(F.CODE[d], 2, 4096, 11008)].startswith("gemv.k")
+    # f4f4 (unit scales, no per-stage scale copies): two accumulators on 256x192
+    assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 2048, 4096, 11008)] == "256x192"
     t16 = G.tile_index("16x128")
     assert G.tile_supported(F.CODE["fp16"], t16, 16, 4096, 11008)
     assert not G.tile_supported(F.CODE["fp16"], t16, 17, 4096, 11008)     # N <= 16
