@@ -1246,8 +1246,10 @@ int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {
   const int nr = pick_nr(N);
   const long ctas = (long)((M + cols_per_cta(dt, N) - 1) / cols_per_cta(dt, N)) *
                     ((N + nr - 1) / nr);
-  // about two CTAs per SM: measured best on the thin row for every dtype
-  const long target = 2L * (num_sms > 0 ? num_sms : 148);
+  // about two CTAs per SM: measured best on the thin row for every dtype but
+  // f4f4, whose CTAs (256 columns, two resident per SM) do best at about one
+  // per SM (gemv.k4 18.4 us against gemv.k8 22.5 us at N=1, K=4096, M=11008)
+  const long target = (dt == kF4F4 ? 1L : 2L) * (num_sms > 0 ? num_sms : 148);
   int s = 1;
   if (ctas > kMaxCounterTiles) {
     while (s < 8 && !gemv_supported(dt, s, N, K, M)) s *= 2;   // cluster splits need no counters

@@ -73,6 +73,7 @@ def test_layout_rules_and_tile_support():
         assert G.tile_names()[G.default_tile(F.CODE[d], 2, 4096, 11008)].startswith("gemv.k")
     # f4f4 (unit scales, no per-stage scale copies): two accumulators on 256x192
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 2048, 4096, 11008)] == "256x192"
+    assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 1, 4096, 11008)] == "gemv.k4"
     t16 = G.tile_index("16x128")
     assert G.tile_supported(F.CODE["fp16"], t16, 16, 4096, 11008)
     assert not G.tile_supported(F.CODE["fp16"], t16, 17, 4096, 11008)     # N <= 16
