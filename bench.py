@@ -65,7 +65,8 @@ BASELINE_METRIC = "TFLOPS/TOPS per dtype×shape at 1/2/4/8 B200; % of tensor-pea
 SUITE = [("square", 4096, 4096, 4096, 50), ("fat", 2048, 4096, 11008, 50), ("thin", 1, 4096, 11008, 100)]
 KIND_RATIO = {"f16": 1.0, "i8": 2.0, "f8f6f4": 2.0, "mxf4": 4.0}
 PROBE_KIND = {"f16": 0, "i8": 1, "f8f6f4": 2, "mxf8f6f4": 3, "mxf4": 4,
-              "f16_pair_bmn": 8, "i8_pair_bmn": 9, "f8f6f4_pair_bmn": 10}
+              "f16_pair_bmn": 8, "i8_pair_bmn": 9, "f8f6f4_pair_bmn": 10,
+              "mxf8f6f4_pair": 11, "mxf4_pair": 12, "mxf8f6f4_pair_cp": 13, "mxf4_pair_cp": 14}
 
 
 def parse():
@@ -471,6 +472,8 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
                 kind_probe = "mxf8f6f4"
             else:
                 kind_probe = kind
+            if kind_probe in ("mxf8f6f4", "mxf4") and tile.startswith("256x"):
+                kind_probe += "_pair"   # block-scaled MMAs on CTA pairs
             windows.append((w.t0, w.t1))
             row = {"shape": sname, "dtype": dtype, "N": N, "K": K, "M": M, "tile": tile,
                    "ms_median": med, "ms_mean": statistics.mean(ms), "iters": iters,
@@ -715,7 +718,8 @@ def ours(a):
                     probe[kname] = G.peak_probe(local, kid, 4096, 5)
             line["probe"] = {k: round(v, 1) for k, v in probe.items()}
             line["probe"]["what"] = ("gemm_peak_probe: tcgen05 MMAs on operands resident in shared memory, one CTA "
-                                     "per SM (pairs: one CTA pair per two SMs; *_bmn: B read MN-major)")
+                                     "per SM (pairs: one CTA pair per two SMs; *_bmn: B read MN-major; "
+                                     "*_cp: with the GEMM's per-stage scale-cell copies)")
             del d, X, W, Y, WSP
             suite, windows = run_suite(G, clk, FL, probe, hbm, bf16, src)
             line["suite"] = {"rows": suite, "n": len(suite), "parity_ok": all(r["parity_ok"] for r in suite),

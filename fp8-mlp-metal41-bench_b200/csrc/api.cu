@@ -591,7 +591,7 @@ int gemm_time_e2e_pipelined(int device, int dtype, int tile, const void* hX, voi
 int gemm_peak_probe(int device, int kind, int reps, int iters, double* tflops_out) {
   DevState* s = dev_state(device);
   if (!s) return fail(GEMM_ERR_INIT, "device %d not initialised", device);
-  if (kind < 0 || kind > 10 || reps < 1 || iters < 1 || !tflops_out) return fail(GEMM_ERR_ARGS, "bad probe arguments");
+  if (kind < 0 || kind > 14 || reps < 1 || iters < 1 || !tflops_out) return fail(GEMM_ERR_ARGS, "bad probe arguments");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   const int ctas = kind >= 5 ? (s->num_sms / 2) * 2 : s->num_sms;

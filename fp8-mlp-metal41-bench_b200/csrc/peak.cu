@@ -15,7 +15,12 @@
 // 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2, M = 256).  Kinds
 // 8 f16 / 9 i8 / 10 f8f6f4 are the pairs again with B read MN-major (the
 // instruction descriptor's transpose-B bit, 128-byte swizzle atoms along N),
-// the operand layout of the [K,M] weights in the GEMM's pair kernel.
+// the operand layout of the [K,M] weights in the GEMM's pair kernel.  Kinds
+// 11 mxf8f6f4 / 12 mxf4 are the block-scaled kinds on CTA pairs (K-major B,
+// unit scale cells copied to TMEM once), and 13 / 14 the same with the GEMM's
+// per-stage scale-cell copies issued before each stage's MMAs (3 for
+// mxf8f6f4, 6 for mxf4: one 32x128b.warpx4 copy per 128 rows x 4 scales of X
+// and of the pair's 256 W columns), into a ring of 4 TMEM slots.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -49,10 +54,10 @@ constexpr uint32_t peak_idesc() {
   return (1u << 7) | (1u << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);   // mxf4
 }
 
-template <int KIND, bool PAIR, bool BMN = false>
+template <int KIND, bool PAIR, bool BMN = false, bool SFCP = false>
 __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* sink, int* dev_err) {
-  static_assert(!PAIR || KIND <= kKindF8F6F4, "pairs: unscaled kinds");
   static_assert(!BMN || PAIR, "MN-major B: pair probes");
+  static_assert(!SFCP || (PAIR && KIND >= kKindMxF8F6F4), "per-stage scale copies: block-scaled pairs");
   // MN-major B as the pair kernel lays it out: boxes of (128 bytes of N) x
   // (one 128-byte K stage), the boxes kBox bytes apart (the descriptor's
   // leading-dimension offset); one MMA's K slice starts kAdv bytes further on
@@ -103,19 +108,37 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* 
   if (warp == 0 && lane == 0 && leader) {
     constexpr uint32_t idesc = peak_idesc<KIND, PAIR, BMN>();
     const uint32_t a = smem_u32(smem), b = a + kA, sf = a + kSfOff;
-    const uint32_t sfa_t = tmem + kPeakN, sfb_t = tmem + kPeakN + 4;
-    if constexpr (KIND >= kKindMxF8F6F4) {
-      tc_cp_32x128b_warpx4(sfa_t, sdesc_plain(sf, 0, 128));
-      for (int c = 0; c < kPeakN / 128; ++c) tc_cp_32x128b_warpx4(sfb_t + 4 * c, sdesc_plain(sf, 0, 128));
-    }
+    // scale cells: slot q of 4 holds 2 cells x (4 A + 8 B columns) after the accumulator
+    constexpr int kCells = KIND == kKindMxF4 ? 2 : 1;
+    auto slot = [&](int q) { return tmem + kPeakN + (uint32_t)(q * 24); };
+    auto copy_cells = [&](uint32_t base) {
+#pragma unroll
+      for (int g = 0; g < kCells; ++g) {
+        const uint32_t t = base + g * 12;
+        if constexpr (PAIR) {
+          tc_cp_pair_32x128b_warpx4(t, sdesc_plain(sf, 0, 128));
+          for (int c = 0; c < kPeakN / 128; ++c) tc_cp_pair_32x128b_warpx4(t + 4 + 4 * c, sdesc_plain(sf, 0, 128));
+        } else {
+          tc_cp_32x128b_warpx4(t, sdesc_plain(sf, 0, 128));
+          for (int c = 0; c < kPeakN / 128; ++c) tc_cp_32x128b_warpx4(t + 4 + 4 * c, sdesc_plain(sf, 0, 128));
+        }
+      }
+    };
+    if constexpr (KIND >= kKindMxF8F6F4) copy_cells(slot(0));
     for (int r = 0; r < reps; ++r) {
+      const uint32_t sfa_t = slot(SFCP ? (r & 3) : 0), sfb_t = sfa_t + 4;
+      if constexpr (SFCP) copy_cells(sfa_t);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint64_t ad = sdesc_sw128(a + kk * 32, 16, 1024);
         const uint64_t bd = BMN ? sdesc_sw128(b + kk * kAdv, kBox, 1024) : sdesc_sw128(b + kk * 32, 16, 1024);
         const uint32_t acc = (r | kk) != 0 ? 1u : 0u;
-        if constexpr (PAIR) tc_mma_pair<KIND>(tmem, ad, bd, idesc, acc);
-        else if constexpr (KIND >= kKindMxF8F6F4) tc_mma_bs<KIND>(tmem, ad, bd, idesc, acc, sfa_t, sfb_t);
+        // the cell of this MMA's K slice (mxf4: two MMAs per cell, as in the GEMM)
+        const uint32_t cell = KIND == kKindMxF4 ? (uint32_t)(kk / 2) * 12u : 0u;
+        if constexpr (PAIR && KIND >= kKindMxF8F6F4)
+          tc_mma_pair_bs<KIND>(tmem, ad, bd, idesc, acc, sfa_t + cell, sfb_t + cell);
+        else if constexpr (PAIR) tc_mma_pair<KIND>(tmem, ad, bd, idesc, acc);
+        else if constexpr (KIND >= kKindMxF8F6F4) tc_mma_bs<KIND>(tmem, ad, bd, idesc, acc, sfa_t + cell, sfb_t + cell);
         else tc_mma<KIND>(tmem, ad, bd, idesc, acc);
       }
     }
@@ -140,9 +163,9 @@ __global__ void __launch_bounds__(kPeakThreads, 1) peak_kernel(int reps, float* 
   }
 }
 
-template <int KIND, bool PAIR, bool BMN = false>
+template <int KIND, bool PAIR, bool BMN = false, bool SFCP = false>
 cudaError_t launch_one(int reps, int ctas, float* sink, int* dev_err, cudaStream_t st) {
-  auto k = peak_kernel<KIND, PAIR, BMN>;
+  auto k = peak_kernel<KIND, PAIR, BMN, SFCP>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -166,7 +189,7 @@ cudaError_t launch_one(int reps, int ctas, float* sink, int* dev_err, cudaStream
 static int peak_kmma(int kind) {
   switch (kind) {
     case 0: case 5: case 8: return 16;
-    case 4: return 64;
+    case 4: case 12: case 14: return 64;
     default: return 32;
   }
 }
@@ -191,6 +214,10 @@ cudaError_t launch_peak(int kind, int reps, int ctas, float* sink, int* dev_err,
     case 8: return launch_one<kKindF16, true, true>(reps, ctas, sink, dev_err, st);
     case 9: return launch_one<kKindI8, true, true>(reps, ctas, sink, dev_err, st);
     case 10: return launch_one<kKindF8F6F4, true, true>(reps, ctas, sink, dev_err, st);
+    case 11: return launch_one<kKindMxF8F6F4, true>(reps, ctas, sink, dev_err, st);
+    case 12: return launch_one<kKindMxF4, true>(reps, ctas, sink, dev_err, st);
+    case 13: return launch_one<kKindMxF8F6F4, true, false, true>(reps, ctas, sink, dev_err, st);
+    case 14: return launch_one<kKindMxF4, true, false, true>(reps, ctas, sink, dev_err, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -435,7 +435,9 @@ PEAK_KINDS = [(0, "tcgen05 kind::f16"), (1, "tcgen05 kind::i8"), (2, "tcgen05 ki
               (3, "tcgen05 kind::mxf8f6f4"), (4, "tcgen05 kind::mxf4"), (5, "tcgen05 kind::f16 x2"),
               (6, "tcgen05 kind::i8 x2"), (7, "tcgen05 kind::f8f6f4 x2"),
               (8, "tcgen05 kind::f16 x2 B MN-major"), (9, "tcgen05 kind::i8 x2 B MN-major"),
-              (10, "tcgen05 kind::f8f6f4 x2 B MN-major")]
+              (10, "tcgen05 kind::f8f6f4 x2 B MN-major"), (11, "tcgen05 kind::mxf8f6f4 x2"),
+              (12, "tcgen05 kind::mxf4 x2"), (13, "kind::mxf8f6f4 x2 + SF copies"),
+              (14, "kind::mxf4 x2 + SF copies")]
 PEAK_REPS = 4096
 
 

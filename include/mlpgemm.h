@@ -239,7 +239,9 @@ int gemm_run_noalloc(int device, int dtype, int ksplit, const void *X, const voi
 /* kind: 0 f16, 1 i8, 2 f8f6f4 (E4M3), 3 mxf8f6f4 (E4M3 x E2M1), 4 mxf4, and
  * 5 f16 / 6 i8 / 7 f8f6f4 on CTA pairs (cta_group::2); 8 f16 / 9 i8 /
  * 10 f8f6f4 on CTA pairs with B read MN-major (the layout of [K,M] weights,
- * as the GEMM's pair tiles read W).  Runs 2 untimed and
+ * as the GEMM's pair tiles read W); 11 mxf8f6f4 / 12 mxf4 on CTA pairs, and
+ * 13 / 14 the same with the GEMM's per-stage scale-cell copies (tcgen05.cp)
+ * before each stage's MMAs.  Runs 2 untimed and
  * `iters` timed launches of a kernel that issues reps x 4 tcgen05.mma
  * (128 x 256 per CTA, or 256 x 256 per pair) on operands resident in shared
  * memory, no global traffic in the loop (tune/peak.metal:29-87), and

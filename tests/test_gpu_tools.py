@@ -29,8 +29,10 @@ pytestmark = pytest.mark.gpu
 
 # probe kind -> dense rate relative to kind::f16 on the same number of SMs
 RATIO = {0: 1.0, 1: 2.0, 2: 2.0, 3: 2.0, 4: 4.0, 5: 1.0, 6: 2.0, 7: 2.0}
-# pair kinds with B MN-major: finite and positive (their rate is what they measure)
-MN_KINDS = (8, 9, 10)
+# pair kinds with B MN-major, and the block-scaled pairs without and with the
+# GEMM's per-stage scale-cell copies: finite and positive (their rate is what
+# they measure)
+MN_KINDS = (8, 9, 10, 11, 12, 13, 14)
 
 
 def test_peak_probe_every_kind(gemm):
@@ -45,9 +47,11 @@ def test_peak_probe_every_kind(gemm):
         r = v / f16
         assert 0.75 * RATIO[k] <= r <= 1.25 * RATIO[k], f"kind {k}: {v:.1f} is {r:.2f}x f16, want ~{RATIO[k]}x"
     mn = {k: gemm.peak_probe(0, k, 4096, 5) for k in MN_KINDS}
-    print("pair probes with B MN-major:", {k: round(v, 1) for k, v in mn.items()})
+    print("pair probes (B MN-major; block-scaled):", {k: round(v, 1) for k, v in mn.items()})
     for k, v in mn.items():
         assert math.isfinite(v) and v > 0, (k, v)
+    # the per-stage scale copies cost MMA time, never add to it
+    assert mn[13] <= 1.05 * mn[11] and mn[14] <= 1.05 * mn[12]
 
 
 def test_peak_probe_rejects_unknown_kind(gemm):
