@@ -54,6 +54,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kThreads = 256;
+constexpr int kBarBytes = 512;   // shared memory reserved for the barrier block (Bars) in every kernel
 constexpr int kRowBytes = 128;   // bytes of K per operand row per stage (one swizzle row)
 constexpr int kSfChunk = 512;    // one 32 x 16-byte scale-factor block (one tcgen05.cp)
 
@@ -182,11 +183,11 @@ struct Cfg {
   static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
   static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + STAGES * SF_COLS_STAGE);
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;    // + barriers + alignment slack
+  static constexpr int SMEM_BYTES = BAR_OFF + kBarBytes + 1024;    // + barriers + alignment slack
   // TMA-store epilogue: 4 KB staging buffers per epilogue warp, two where the
   // shared-memory budget allows (a chunk's store overlaps the next chunk's
   // staging), else one
-  static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
+  static constexpr int EPI_OFF = (BAR_OFF + kBarBytes + 1023) / 1024 * 1024;
   static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448 ? 2 : 1;
   static constexpr int SMEM_EPI = EPI_OFF + 4 * EPI_BUFS * 4096 + 1024;
   static constexpr uint32_t IDESC =
@@ -217,7 +218,9 @@ struct Bars {
   uint32_t tmem_base;
   int abort_flag;
   uint64_t sf_ready[8];   // block-scaled kinds: a stage's scale cells are in TMEM
+  uint64_t sf_free[8];    // block-scaled pair tiles with fewer TMEM scale slots than stages
 };
+static_assert(sizeof(Bars) <= kBarBytes, "barrier block");
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int& tm, int& tn) {
   tm = tile % tiles_m;
@@ -441,14 +444,15 @@ __device__ __forceinline__ void drain_quadrant(uint32_t taddr0, uint32_t* yrow, 
     if (!row_ok) return;
     store_row(r, cb);
   };
-  static_assert(NCH % 2 == 0, "chunks come in pairs");
   uint32_t ra[32], rb[32];
   tmem_ld_32x32b_x32(taddr0, ra);
 #pragma unroll 1
   for (int c = 0; c < NCH; c += 2) {
     tmem_ld_wait();                                            // chunk c in ra
-    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 1) * 32), rb);
+    if (c + 1 < NCH) tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 1) * 32), rb);
+    else release();                                            // an odd last chunk
     store(ra, c);
+    if (c + 1 >= NCH) break;
     tmem_ld_wait();                                            // chunk c + 1 in rb
     if (c + 2 < NCH) tmem_ld_32x32b_x32(taddr0 + (uint32_t)((c + 2) * 32), ra);
     else release();
@@ -476,7 +480,6 @@ __device__ __forceinline__ void drain_quadrant_tma(uint32_t taddr0, int col0, in
                                                    Release release, unsigned char* epi, const EpiMaps* em,
                                                    int& nst) {
   static_assert(NBUF >= 1 && NBUF <= 2, "one or two staging buffers");
-  static_assert(NCH % 2 == 0, "chunks come in pairs");
   const int lane = (int)(threadIdx.x & 31u);
   auto put = [&](uint32_t (&r)[32], int c) {
     const int cb = col0 + c * 32;
@@ -502,12 +505,13 @@ __device__ __forceinline__ void drain_quadrant_tma(uint32_t taddr0, int col0, in
     ++nst;
   };
   // TMEM loads in groups of two chunks (two 32-column loads in flight per wait),
-  // double-buffered: group g + 1 loads while group g is staged and stored
-  constexpr int NG = NCH / 2;
+  // double-buffered: group g + 1 loads while group g is staged and stored; an
+  // odd chunk count ends with a group of one
+  constexpr int NG = (NCH + 1) / 2;
   uint32_t ra0[32], ra1[32], rb0[32], rb1[32];
   auto load_group = [&](int g, uint32_t (&x0)[32], uint32_t (&x1)[32]) {
     tmem_ld_32x32b_x32(taddr0 + (uint32_t)((2 * g) * 32), x0);
-    tmem_ld_32x32b_x32(taddr0 + (uint32_t)((2 * g + 1) * 32), x1);
+    if (2 * g + 1 < NCH) tmem_ld_32x32b_x32(taddr0 + (uint32_t)((2 * g + 1) * 32), x1);
   };
   load_group(0, ra0, ra1);
 #pragma unroll 1
@@ -516,13 +520,13 @@ __device__ __forceinline__ void drain_quadrant_tma(uint32_t taddr0, int col0, in
     if (g + 1 < NG) load_group(g + 1, rb0, rb1);
     else release();
     put(ra0, 2 * g);
-    put(ra1, 2 * g + 1);
+    if (2 * g + 1 < NCH) put(ra1, 2 * g + 1);
     if (g + 1 >= NG) break;
     tmem_ld_wait();                                            // group g + 1 in rb
     if (g + 2 < NG) load_group(g + 2, ra0, ra1);
     else release();
     put(rb0, 2 * g + 2);
-    put(rb1, 2 * g + 3);
+    if (2 * g + 3 < NCH) put(rb1, 2 * g + 3);
   }
 }
 
@@ -864,10 +868,15 @@ struct Cfg2 {
   static constexpr int SF_STAGE_BYTES = SF_A_BYTES + SF_B_BYTES;
   static constexpr int SF_COLS_A = 4, SF_COLS_B = 4 * SF_B_CHUNKS;
   static constexpr int SF_COLS_STAGE = SF_CELLS * (SF_COLS_A + SF_COLS_B);
-  // two accumulators where they fit beside the ring's scale cells in the 512
-  // TMEM columns (a 256x192 scaled tile: 384 + 5 x 24); one for 256-wide scaled
-  // tiles, whose two accumulators would leave no column for the scales
-  static constexpr int ACC_BUFS = (!SCALED || 2 * BN + STAGES * SF_COLS_STAGE <= 512) ? 2 : 1;
+  // TMEM scale slots: one per ring stage where they fit beside two
+  // accumulators in the 512 TMEM columns (a 256x192 scaled tile: 384 + 5 x 24);
+  // else at least two, each reused once the MMAs of the stage that held it have
+  // completed (sf_free: a 256x224 mxf4 tile, 448 + 2 x 24).  256-wide scaled
+  // tiles, whose two accumulators would leave no column for the scales, keep a
+  // slot per stage and one accumulator.
+  static constexpr int SF_FIT = SCALED ? (512 - 2 * BN) / SF_COLS_STAGE : 0;
+  static constexpr int SF_SLOTS = !SCALED ? 0 : (SF_FIT >= STAGES ? STAGES : (SF_FIT >= 2 ? SF_FIT : STAGES));
+  static constexpr int ACC_BUFS = (!SCALED || 2 * BN + SF_SLOTS * SF_COLS_STAGE <= 512) ? 2 : 1;
   static constexpr int K_PER_STAGE = kRowBytes * 8 / T::a_bits;
   static constexpr int MMA_K_BYTES = 32;
   static constexpr int MMAS_PER_STAGE = kRowBytes / MMA_K_BYTES;
@@ -878,20 +887,20 @@ struct Cfg2 {
   static constexpr uint32_t B_ADV = T::b_mn ? (uint32_t)(MMA_K_BYTES * 8 / T::b_bits) * kRowBytes
                                             : (uint32_t)MMA_K_BYTES;
   static constexpr int SF_COL0 = ACC_BUFS * BN;
-  static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + STAGES * SF_COLS_STAGE);
+  static constexpr uint32_t TMEM_COLS = pow2_cols(ACC_BUFS * BN + SF_SLOTS * SF_COLS_STAGE);
   static constexpr int SF_OFF = STAGES * STAGE_BYTES;
   static constexpr int SF_CONST_OFF = SF_OFF + STAGES * SF_STAGE_BYTES;   // 512 bytes of 127s
   static constexpr int BAR_OFF = SF_CONST_OFF + (SCALED ? kSfChunk : 0);
   // TMA-store epilogue: 4 KB staging buffers per epilogue warp, two where the
   // shared-memory budget allows, else one; none (plain stores) if even one
   // does not fit beside the ring
-  static constexpr int EPI_OFF = (BAR_OFF + 256 + 1023) / 1024 * 1024;
+  static constexpr int EPI_OFF = (BAR_OFF + kBarBytes + 1023) / 1024 * 1024;
   static constexpr int EPI_BUFS = EPI_OFF + 4 * 2 * 4096 + 1024 <= 232448   ? 2
                                   : EPI_OFF + 4 * 1 * 4096 + 1024 <= 232448 ? 1
                                                                             : 0;
   static constexpr bool EPI_TMA = EPI_BUFS > 0;
-  static constexpr int SMEM_BYTES = (EPI_TMA ? EPI_OFF + 4 * EPI_BUFS * 4096 : BAR_OFF + 256) + 1024;
-  static constexpr int SMEM_BASE = BAR_OFF + 256 + 1024;   // launches with plain epilogue stores
+  static constexpr int SMEM_BYTES = (EPI_TMA ? EPI_OFF + 4 * EPI_BUFS * 4096 : BAR_OFF + kBarBytes) + 1024;
+  static constexpr int SMEM_BASE = BAR_OFF + kBarBytes + 1024;   // launches with plain epilogue stores
   static constexpr uint32_t IDESC =
       SCALED ? ((T::a_fmt << 7) | (T::b_fmt << 10) | ((uint32_t)(BN >> 3) << 17) | (1u << 23) |
                 ((uint32_t)(256 >> 4) << 24))
@@ -901,7 +910,8 @@ struct Cfg2 {
   static constexpr bool HALVES = !SCALED && !B_UNPACK && (!T::b_mn || (BH / 2) % B_BOX_MN == 0);
   static constexpr int STAGE_TX_H = A_BYTES + B_BYTES / 2;
   static constexpr uint32_t IDESC_H = (IDESC & ~(0x3Fu << 17)) | ((uint32_t)(BN / 2 >> 3) << 17);
-  static_assert(ACC_BUFS * BN + STAGES * SF_COLS_STAGE <= 512, "TMEM budget");
+  static_assert(ACC_BUFS * BN + SF_SLOTS * SF_COLS_STAGE <= 512, "TMEM budget");
+  static_assert(SF_SLOTS <= 8, "sf_free barriers");
   static_assert(!T::b_mn || BH % B_BOX_MN == 0, "W half-tile must be whole swizzle atoms");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -933,8 +943,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->acc_full[b], 1);
       mbar_init(&bars->acc_empty[b], 2 * 4);            // one arrival per epilogue warp, both CTAs
     }
-    if constexpr (C::SCALED)
+    if constexpr (C::SCALED) {
       for (int st = 0; st < STAGES; ++st) mbar_init(&bars->sf_ready[st], 1);   // leader's copier
+      for (int sl = 0; sl < C::SF_SLOTS; ++sl) mbar_init(&bars->sf_free[sl], 1);
+    }
     bars->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -1024,16 +1036,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // loop measured 7-14 % slower: that single thread paces the scaled tiles.
     // (an operand without a scale plane has unit cells, which the MMA issuer
     // copies into every slot once; with no plane at all this thread has no work)
-    uint32_t stage = 0, phase = 0;
+    // (with fewer TMEM slots than stages, a slot is rewritten once the MMAs of
+    // the stage that last used it have completed: sf_free)
+    uint32_t stage = 0, phase = 0, slot = 0, sphase = 0;
     bool ok = true;
     const bool work = p.sfa || p.sfb;
     const uint32_t smem_base = smem_u32(smem);
     for (int item = pair; work && item < num_items && ok; item += npairs) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&bars->full[stage], phase, ctl, 0x500 + stage)) { ok = false; break; }
+        if constexpr (C::SF_SLOTS < STAGES)
+          if (!mbar_wait(&bars->sf_free[slot], sphase ^ 1u, ctl, 0x600 + slot)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sf_smem = smem_base + C::SF_OFF + stage * C::SF_STAGE_BYTES;
-        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
+        const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + slot * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
           const uint32_t sfa_t = sf_tmem + g * (C::SF_COLS_A + C::SF_COLS_B);
@@ -1048,6 +1064,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit_pair(&bars->sf_ready[stage], 0x1);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if (++slot == (uint32_t)C::SF_SLOTS) { slot = 0; sphase ^= 1u; }
       }
     }
     aborted_any = !ok;
@@ -1062,7 +1079,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // plane go into every ring slot of both CTAs once; this thread's MMAs
       // follow them in issue order
       const uint32_t sf_const = smem_base + C::SF_CONST_OFF;
-      for (int st = 0; st < STAGES; ++st) {
+      for (int st = 0; st < C::SF_SLOTS; ++st) {
         const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + st * C::SF_COLS_STAGE);
 #pragma unroll
         for (int g = 0; g < C::SF_CELLS; ++g) {
@@ -1077,6 +1094,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     const bool via_copier = C::SCALED && (p.sfa || p.sfb);
+    uint32_t slot = 0;   // TMEM scale slot of the stage
     for (int item = pair; item < num_items && ok; item += npairs, ++local) {
       const int buf = C::ACC_BUFS == 2 ? (local & 1) : 0;
       const uint32_t acc_par = C::ACC_BUFS == 2 ? (uint32_t)(local >> 1) & 1u : (uint32_t)local & 1u;
@@ -1092,7 +1110,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_addr = smem_base + stage * C::STAGE_BYTES;
         const uint32_t b_addr = a_addr + C::A_BYTES;
         if constexpr (C::SCALED) {
-          const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + stage * C::SF_COLS_STAGE);
+          const uint32_t sf_tmem = tmem_base + (uint32_t)(C::SF_COL0 + slot * C::SF_COLS_STAGE);
 #pragma unroll
           for (int kk = 0; kk < C::MMAS_PER_STAGE; ++kk) {
             constexpr int per_cell = 4 / T::nsf;
@@ -1113,7 +1131,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tc_commit_pair(&bars->empty[stage], 0x3);
+        if constexpr (C::SCALED && C::SF_SLOTS < STAGES) {
+          if (via_copier) tc_commit_pair(&bars->sf_free[slot], 0x1);   // this slot's MMAs, then its reuse
+        }
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if constexpr (C::SCALED) {
+          if (++slot == (uint32_t)C::SF_SLOTS) slot = 0;
+        }
       }
       if (!ok) break;
       tc_commit_pair(&bars->acc_full[buf], 0x3);
@@ -1224,7 +1248,7 @@ struct WCfg {
   static constexpr uint32_t B_ADV = WT::b_mn ? 16u * kRowBytes : 32u;
   static constexpr uint32_t TMEM_COLS = pow2_cols(2 * BN);
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int SMEM_BYTES = BAR_OFF + kBarBytes + 1024;
   static constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | ((WT::b_mn ? 1u : 0u) << 16) |
                                     ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
   static_assert(STAGE_BYTES % 1024 == 0, "swizzle atoms need 1 KB alignment");
@@ -1896,7 +1920,7 @@ cudaError_t launch_widen(const RunArgs& a) {
 
 bool tc_supported(int dt, int bm, int bn, int N, int K, int M) {
   if (N <= 0 || K <= 0 || M <= 0) return false;
-  if (bn == 192) {   // CTA pairs, 256x192: the block-scaled kinds (two accumulators)
+  if (bn == 192 || bn == 224) {   // CTA pairs, 256x192 / 256x224: the block-scaled kinds (two accumulators)
     if (bm != 256) return false;
     if (dt == kMX4X4) return K % 32 == 0;
     if (dt == kF4F4) return K % 32 == 0 && M % 2 == 0;
@@ -2093,6 +2117,15 @@ cudaError_t launch_tc(const RunArgs& a, int bm, int bn) {
   for (int i = 0; i < a.npeers; ++i)
     if (!a.ypeers || !aligned(a.ypeers[i], 16)) return cudaErrorInvalidValue;
   if (!aligned(a.X, 16) || !aligned(a.W, 32) || !aligned(a.Y, 16)) return cudaErrorInvalidValue;
+  if (bm == 256 && bn == 224) {   // block-scaled kinds, two accumulators (TMEM scale slots reused)
+    switch (a.dt) {
+      case kF4F4: return launch_f4f4_pair<224>(a);
+      case kMX4X4: return launch_scaled_pair<kMX4X4, 224>(a);
+      case kMX8X4: return launch_scaled_pair<kMX8X4, 224>(a);
+      case kF8X4: return launch_scaled_pair<kF8X4, 224>(a);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (bm == 256 && bn == 192) {   // block-scaled kinds, two accumulators
     switch (a.dt) {
       case kF4F4: return launch_f4f4_pair<192>(a);

@@ -71,8 +71,10 @@ def test_layout_rules_and_tile_support():
     for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8"):
         assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "gemv.mma"
         assert G.tile_names()[G.default_tile(F.CODE[d], 2, 4096, 11008)].startswith("gemv.k")
-    # f4f4 (unit scales, no per-stage scale copies): two accumulators on 256x192
-    assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 2048, 4096, 11008)] == "256x192"
+    # f4f4 and mxfp4/f8 (unit scale cells copied once): two accumulators on 256x224
+    assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 2048, 4096, 11008)] == "256x224"
+    assert G.tile_names()[G.default_tile(F.CODE["mxfp4/f8"], 2048, 4096, 11008)] == "256x224"
+    assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a4"], 2048, 4096, 11008)] == "256x256"
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 1, 4096, 11008)] == "gemv.k4"
     t16 = G.tile_index("16x128")
     assert G.tile_supported(F.CODE["fp16"], t16, 16, 4096, 11008)

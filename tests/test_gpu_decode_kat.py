@@ -37,7 +37,7 @@ E4M3_FINITE = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.u
 HALF_FINITE = np.array([c for c in range(65536) if (c & 0x7C00) != 0x7C00], dtype=np.uint16)
 
 TC_TILES = ["256x256", "128x256", "128x128"]
-SCALED_192 = {"f4f4", "mxfp4/a4", "mxfp4/a8", "mxfp4/f8"}   # 256x192 CTA pairs
+SCALED_192 = {"f4f4", "mxfp4/a4", "mxfp4/a8", "mxfp4/f8"}   # 256x192 and 256x224 CTA pairs
 THIN_TC = {"fp16", "int8", "i8i8", "fp8", "f8f8", "mxfp4"}
 GEMV_TILES = ["gemv.k1", "gemv.k8"]
 
@@ -155,7 +155,7 @@ def assert_bit_exact(dtype, out, ref, what):
 def _cases():
     out = []
     for d in F.DTYPES:
-        tiles = TC_TILES + (["256x192"] if d in SCALED_192 else []) + (["16x128"] if d in THIN_TC else []) + GEMV_TILES
+        tiles = TC_TILES + (["256x192", "256x224"] if d in SCALED_192 else []) + (["16x128"] if d in THIN_TC else []) + GEMV_TILES
         for t in tiles:
             for r in MX_RANGES.get(d, [None]):
                 out.append((d, t, r))
@@ -174,7 +174,7 @@ def test_one_hot_decode_is_bit_exact(gemm, dtype, tile, srange):
 # E4M3 NaN codes (0x7F, 0xFF) decode to NaN (main.swift:33): a NaN weight makes
 # its whole output column NaN (0 * NaN is NaN), a NaN activation its whole row.
 NAN_CASES = [(d, t) for d in ("fp8", "f8f8") for t in TC_TILES + ["16x128"] + GEMV_TILES]
-NAN_CASES += [(d, t) for d in ("mxfp4/a8", "mxfp4/f8") for t in TC_TILES + ["256x192"] + GEMV_TILES]
+NAN_CASES += [(d, t) for d in ("mxfp4/a8", "mxfp4/f8") for t in TC_TILES + ["256x192", "256x224"] + GEMV_TILES]
 
 
 @pytest.mark.parametrize("dtype,tile", NAN_CASES)

@@ -61,9 +61,11 @@ def assert_close(dtype, out, ref):
 TC_TILES = {d: ["256x256", "128x256", "128x128"] for d in ("fp16", "i8i8", "f8f8")}
 TC_TILES.update({d: ["256x256", "128x256", "128x128"] for d in ("int8", "fp8")})   # 256x256: W widened once
 TC_TILES.update({"mxfp4": ["256x256", "128x256", "128x128"]})   # 256x256: widened once to f16 [K,M]
-# block-scaled kinds (and f4f4 on kind::mxf4) also run 256x192 CTA pairs with two accumulators
-TC_TILES.update({"f4f4": ["256x256", "256x192", "128x256", "128x128"]})
-TC_TILES.update({d: ["256x256", "256x192", "128x256", "128x128"] for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
+# block-scaled kinds (and f4f4 on kind::mxf4) also run 256x192 and 256x224 CTA pairs with two
+# accumulators (256x224 mxf4: two TMEM scale slots reused across the ring's stages)
+TC_TILES.update({"f4f4": ["256x256", "256x192", "256x224", "128x256", "128x128"]})
+TC_TILES.update({d: ["256x256", "256x192", "256x224", "128x256", "128x128"]
+                 for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8")})
 TC_CASES = [(d, t) for d in F.DTYPES for t in TC_TILES[d]]
 
 
@@ -487,4 +489,14 @@ def test_default_tile_mx_quantized_x(gemm, dtype, N):
     ti = gemm.default_tile(F.CODE[dtype], N, K, M)
     assert gemm.tile_names()[ti] == "gemv.mma"
     out, ref, _ = run_case(gemm, dtype, "gemv.mma", N, K, M)
+    assert_close(dtype, out, ref)
+
+
+@pytest.mark.parametrize("dtype", ["mxfp4/a4", "mxfp4/a8", "f4f4"])
+def test_pair_224_long_k(gemm, dtype):
+    # 256x224 at K = 4096: 16 (mxf4) or 32 (mxf8f6f4) stages per tile, so the
+    # mxf4 tile's two TMEM scale slots are rewritten many times per tile, over
+    # two tile rows and a part-filled last column tile (2000 = 8 x 224 + 208)
+    N, K, M = 512, 4096, 2000
+    out, ref, _ = run_case(gemm, dtype, "256x224", N, K, M)
     assert_close(dtype, out, ref)
