@@ -280,7 +280,7 @@ __device__ __forceinline__ void stream_emit(const GemvParams& p, const Acc* red,
 // a warp and in shared memory across warps, in a fixed order; K splits in a
 // cluster (reduce_splits).
 template <int DT, int NR, int LW, int CL, int U>
-__global__ void __launch_bounds__(kThreads, (NR == 1 && DT != kF4F4) ? 4 : 2) gemv_mn_split_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kThreads, NR == 1 ? 4 : 2) gemv_mn_split_kernel(GemvParams p) {
   using Acc = std::conditional_t<DT == kI8I8, int, float>;
   constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights (columns) per thread
   constexpr int CPC = CL * E;                   // columns per CTA
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, (NR == 1 && DT != kF4F4) ? 4 : 2) ge
 // (slab, row-group) units with two cursors; the split form above serves the
 // K-split tiles.
 template <int DT, int NR, int LW, int CL, int U, bool STREAM>
-__global__ void __launch_bounds__(kThreads, (NR == 1 && DT != kF4F4) ? 4 : 2) gemv_mn_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kThreads, NR == 1 ? 4 : 2) gemv_mn_kernel(GemvParams p) {
   using Acc = std::conditional_t<DT == kI8I8, int, float>;
   constexpr int E = LW * 2 / w_bytes_x2<DT>();  // weights (columns) per thread
   constexpr int CPC = CL * E;                   // columns per CTA
@@ -1045,22 +1045,25 @@ constexpr size_t kMaxGemvSmem = 227 * 1024;
 // stream-K: grid bound (persistent CTAs) and the partial-slot layout sized by it
 constexpr int kMaxStreamCtas = 1024;
 
-// Bytes loaded per thread per weight row, so that NR * E <= 64 accumulators.
-template <int DT>
-constexpr int pick_lw(int NR) {
-  constexpr int bx2 = w_bytes_x2<DT>();
+// Bytes loaded per thread per weight row (16, 8 or 4), so that NR * E stays
+// within the accumulator budget: 64, or 16 for f4f4, whose 32 columns per
+// 16 bytes would otherwise hold the kernel to two CTAs per SM (one wave of
+// gemv.k4 then had 1.16 CTAs per SM; 8-byte chunks fit four per SM).
+__host__ __device__ constexpr int lw_for(int dt, int nr) {
+  const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
+  const int cap = dt == kF4F4 ? 16 : 64;
   int lw = 16;
-  while (lw > 4 && NR * (lw * 2 / bx2) > 64) lw /= 2;
+  while (lw > 4 && nr * (lw * 2 / bx2) > cap) lw /= 2;
   return lw;
 }
 
+template <int DT>
+constexpr int pick_lw(int NR) { return lw_for(DT, NR); }
+
 int cols_per_cta(int dt, int N) {
   if (w_is_mx(dt)) return kWarps * (32 / kLanesPerMxRow);
-  const int nr = pick_nr(N);
   const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
-  int lw = 16;
-  while (lw > 4 && nr * (lw * 2 / bx2) > 64) lw /= 2;
-  return kLanesPerRow * (lw * 2 / bx2);
+  return kLanesPerRow * (lw_for(dt, pick_nr(N)) * 2 / bx2);
 }
 
 // Workspace layout: [kCounterBytes of tile counters][ksplit * N * M partials].
@@ -1246,10 +1249,8 @@ int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {
   const int nr = pick_nr(N);
   const long ctas = (long)((M + cols_per_cta(dt, N) - 1) / cols_per_cta(dt, N)) *
                     ((N + nr - 1) / nr);
-  // about two CTAs per SM: measured best on the thin row for every dtype but
-  // f4f4, whose CTAs (256 columns, two resident per SM) do best at about one
-  // per SM (gemv.k4 18.4 us against gemv.k8 22.5 us at N=1, K=4096, M=11008)
-  const long target = (dt == kF4F4 ? 1L : 2L) * (num_sms > 0 ? num_sms : 148);
+  // about two CTAs per SM: measured best on the thin row for every dtype
+  const long target = 2L * (num_sms > 0 ? num_sms : 148);
   int s = 1;
   if (ctas > kMaxCounterTiles) {
     while (s < 8 && !gemv_supported(dt, s, N, K, M)) s *= 2;   // cluster splits need no counters
@@ -1336,10 +1337,8 @@ bool stream_supported(int dt, int N, int K, int M) {
   if (N < 1 || N > 16 || K < 1 || M < 1) return false;
   if (!w_is_mx(dt)) {
     // every thread's 16/8/4-byte chunk is whole and aligned on every row
-    const int nr = pick_nr(N);
     const int bx2 = dt == kFP16 ? 4 : (dt == kF4F4 ? 1 : 2);
-    int lw = 16;
-    while (lw > 4 && nr * (lw * 2 / bx2) > 64) lw /= 2;
+    const int lw = lw_for(dt, pick_nr(N));
     const int e = lw * 2 / bx2;
     if (((long)M * bx2) % 2 != 0 || M % e != 0) return false;
     if (((long)M * bx2 / 2) % lw != 0) return false;
