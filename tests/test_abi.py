@@ -76,6 +76,26 @@ def test_layout_rules_and_tile_support():
     assert G.tile_names()[G.default_tile(F.CODE["mxfp4/f8"], 2048, 4096, 11008)] == "256x224"
     assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a4"], 2048, 4096, 11008)] == "256x256"
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 1, 4096, 11008)] == "gemv.k4"
+    # 256x224 (two accumulators): the block-scaled kinds and f4f4 only
+    t224 = G.tile_index("256x224")
+    for d in ("mxfp4/a4", "f4f4"):
+        assert G.tile_supported(F.CODE[d], t224, 2048, 4096, 11008)
+    assert G.tile_supported(F.CODE["mxfp4/a8"], t224, 2048, 4096, 11008)
+    assert not G.tile_supported(F.CODE["mxfp4/a8"], t224, 2048, 4064, 11008)   # K % 128
+    for d in ("fp16", "i8i8", "f8f8", "int8", "mxfp4"):
+        assert not G.tile_supported(F.CODE[d], t224, 2048, 4096, 11008), d
+    # gemv.mma: N <= 16; [K,M] kinds need K % 4 and 16-byte rows, the MX kinds K % 128
+    tm = G.tile_index("gemv.mma")
+    assert G.tile_supported(F.CODE["int8"], tm, 1, 4096, 11008)
+    assert G.tile_supported(F.CODE["fp16"], tm, 16, 4096, 11008)
+    assert not G.tile_supported(F.CODE["fp16"], tm, 17, 4096, 11008)
+    assert not G.tile_supported(F.CODE["int8"], tm, 1, 4094, 11008)
+    assert not G.tile_supported(F.CODE["int8"], tm, 1, 4096, 11000)
+    assert G.tile_supported(F.CODE["mxfp4/a4"], tm, 8, 4096, 1000)
+    assert not G.tile_supported(F.CODE["mxfp4/a4"], tm, 8, 4064, 1000)
+    assert not G.tile_supported(F.CODE["i8i8"], tm, 1, 4096, 11008)
+    assert not G.tile_supported(F.CODE["f4f4"], tm, 1, 4096, 11008)
+    assert G.workspace_size(F.CODE["int8"], tm, 1, 4096, 11008) > 65536
     t16 = G.tile_index("16x128")
     assert G.tile_supported(F.CODE["fp16"], t16, 16, 4096, 11008)
     assert not G.tile_supported(F.CODE["fp16"], t16, 17, 4096, 11008)     # N <= 16
