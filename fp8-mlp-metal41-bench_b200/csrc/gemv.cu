@@ -1249,13 +1249,31 @@ int gemv_auto_ksplit(int dt, int N, int K, int M, int num_sms) {
   const int nr = pick_nr(N);
   const long ctas = (long)((M + cols_per_cta(dt, N) - 1) / cols_per_cta(dt, N)) *
                     ((N + nr - 1) / nr);
-  // about two CTAs per SM: measured best on the thin row for every dtype
-  const long target = 2L * (num_sms > 0 ? num_sms : 148);
+  const long sms = num_sms > 0 ? num_sms : 148;
   int s = 1;
   if (ctas > kMaxCounterTiles) {
     while (s < 8 && !gemv_supported(dt, s, N, K, M)) s *= 2;   // cluster splits need no counters
     return s;
   }
+  if (nr >= 2 && !w_is_mx(dt)) {
+    // [K,M] weights, two or more rows per CTA: at most 2048 K rows per CTA and
+    // at least one CTA per SM at N = 2, three from N = 3 on.  Measured (us):
+    //   K = 4096, M = 11008, N = 2: two splits for every kind (int8 24.2
+    //     against 26.9 at four, fp16 24.6 against 30.4 at one, f4f4 24.8
+    //     against 36.3 at one); f4f4 N = 4 and 8: four (43.2 against 49.5
+    //     at two, 69.0 against 79.8);
+    //   K = 11008, M = 4096, N = 2: eight (int8 20.8 against 25.4 at
+    //     sixteen, f4f4 21.5 against 23.2; fp16 runs 26.6 at four and 32.0
+    //     at eight); f4f4 N = 4: eight (38.9; sixteen 43.7)
+    const long target = nr == 2 ? sms : 3 * sms;
+    while (s < 64 && (((ctas * s < target || K / s > 2048) && K / (2 * s) >= 64) ||
+                      !gemv_supported(dt, s, N, K, M)))
+      s *= 2;
+    return s;
+  }
+  // one row per CTA (four CTAs per SM) and the [M,K] MX kinds: about two CTAs
+  // per SM, measured best on the N = 1 thin row for every dtype
+  const long target = 2L * sms;
   while (s < 64 && ((ctas * s < target && K / (2 * s) >= 64) || !gemv_supported(dt, s, N, K, M))) s *= 2;
   return s;
 }

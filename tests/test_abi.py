@@ -76,6 +76,16 @@ def test_layout_rules_and_tile_support():
     assert G.tile_names()[G.default_tile(F.CODE["mxfp4/f8"], 2048, 4096, 11008)] == "256x224"
     assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a4"], 2048, 4096, 11008)] == "256x256"
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 1, 4096, 11008)] == "gemv.k4"
+    # [K,M] GEMVs with two or more rows per CTA: at most 2048 K rows per CTA,
+    # at least one CTA per SM at N = 2 and three from N = 3 on (f4f4 has no
+    # tensor-core thin tile)
+    for d in ("fp16", "int8", "i8i8", "fp8", "f8f8", "f4f4"):
+        assert G.tile_names()[G.default_tile(F.CODE[d], 2, 4096, 11008)] == "gemv.k2", d
+        assert G.tile_names()[G.default_tile(F.CODE[d], 2, 11008, 4096)] == "gemv.k8", d
+    for N in (3, 4, 8):
+        assert G.tile_names()[G.default_tile(F.CODE["f4f4"], N, 4096, 11008)] == "gemv.k4"
+        assert G.tile_names()[G.default_tile(F.CODE["f4f4"], N, 11008, 4096)] == "gemv.k8"
+    assert G.tile_names()[G.default_tile(F.CODE["mxfp4"], 2, 4096, 11008)] == "gemv.k1"
     # 256x224 (two accumulators): the block-scaled kinds and f4f4 only
     t224 = G.tile_index("256x224")
     for d in ("mxfp4/a4", "f4f4"):

@@ -130,6 +130,18 @@ def test_suite_thin_row(gemm, dtype):
     assert_close(dtype, out, ref)
 
 
+@pytest.mark.parametrize("dtype,N", [(d, 2) for d in ("fp16", "int8", "i8i8", "fp8", "f8f8", "f4f4")] +
+                         [("f4f4", 4), ("f4f4", 8)])
+def test_default_thin_tile_two_or_more_rows(gemm, dtype, N):
+    # [K,M] weights at 2 <= N with the default split (two at N = 2, four for
+    # f4f4 from N = 3 on): cluster-reduced K splits match the oracle
+    K, M = 4096, 11008
+    tile = gemm.tile_names()[gemm.default_tile(F.CODE[dtype], N, K, M)]
+    assert tile == ("gemv.k2" if N == 2 else "gemv.k4")
+    out, ref, _ = run_case(gemm, dtype, tile, N, K, M)
+    assert_close(dtype, out, ref)
+
+
 def test_gemv_deterministic_and_counters_reset(gemm):
     # two calls on one workspace: identical bits (fixed reduction order) and
     # the split-K counters are back at zero for the second call
