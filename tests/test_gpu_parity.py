@@ -112,6 +112,16 @@ def test_gemv_thin_rows(gemm, dtype, tile):
     assert_close(dtype, out, ref)
 
 
+@pytest.mark.parametrize("dtype", [d for d in F.DTYPES if d in F.W_MX])
+@pytest.mark.parametrize("N,K,M", [(1, 4096, 11008), (2, 4096, 11008), (1, 16384, 3001), (2, 8192, 12000)])
+def test_mx_thin_rows_one_split(gemm, dtype, N, K, M):
+    # gemv.k1 on [M,K] weights at N <= 2 (the kernel that keeps every lane's
+    # weight blocks in flight): the suite's thin row at one and two rows of
+    # X, a long K, and two rows at a ragged M
+    out, ref, _ = run_case(gemm, dtype, "gemv.k1", N, K, M)
+    assert_close(dtype, out, ref)
+
+
 @pytest.mark.parametrize("dtype", F.DTYPES)
 @pytest.mark.parametrize("N", [2, 5, 16])
 def test_gemv_ragged(gemm, dtype, N):
