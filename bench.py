@@ -25,6 +25,8 @@ The JSON line (rank 0) carries, besides the contract's keys:
   roofline   the GEMM kernel against the measured peak (MEASURED_PEAKS.json)
   clocks     NVML SM clock and throttle reasons sampled every 0.5 ms while any
              timed GPU region runs (warm-up, timed steps and the suite), per rank
+  sharded_suite (N > 1) every dtype at the fat shape, M-sharded like the
+             headline, cold L2, max over ranks, parity on every rank
   sharded    (N > 1) the collectives beside the GEMM, timed separately: NCCL
              broadcast of X, NCCL all-gather of the M-sharded Y + permute, the
              N-sharded GEMM with its in-place NCCL all-gather, and the fused
@@ -81,7 +83,8 @@ def parse():
     ap.add_argument("--M", type=int, default=11008)
     ap.add_argument("--tile", default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-suite", action="store_true", help="skip the 30-row suite and the peak probe")
+    ap.add_argument("--no-suite", action="store_true",
+                    help="skip the 30-row suite and the peak probe (N = 1) or the sharded fat-row suite (N > 1)")
     ap.add_argument("--no-gathers", action="store_true")
     return ap.parse_args()
 
@@ -510,6 +513,69 @@ def run_suite(G, clk, FL, probe, hbm, bf16, src):
     return rows, windows
 
 
+def run_sharded_suite(G, torch, dist, world, rank, local, clk, FL, bf16, src, iters=20):
+    """Every dtype at the suite's fat shape (N=2048, K=4096, M=11008), M-sharded
+    across the job's GPUs as the headline is: each rank runs its column block
+    (shard_columns, 32-column aligned) on its default tile with a cold L2 and
+    takes the median of `iters` event-timed launches; the job's time is the
+    max over ranks and value = 2NKM / that time.  Whole rows of every rank's
+    block are checked against an fp64 numpy dot product.  Every rank takes the
+    same single all-reduce per dtype whatever happened on it, so an error on
+    one rank is reported in the row instead of leaving the others waiting."""
+    from mlpgemm import formats as F
+    from mlpgemm.data import Operands, shard_columns
+    from mlpgemm.shard import shard_plan
+    N, K, M = 2048, 4096, 11008
+    plan = shard_plan(M, world)
+    m0, width = plan[rank]
+    names = G.tile_names()
+    ops = Operands(N, K, M, "seeded", 0)
+    rows, windows = [], []
+    for dtype in F.DTYPES:
+        dt = F.CODE[dtype]
+        med, ok, rel, err, tile = float("inf"), False, float("inf"), "", ""
+        try:
+            ti = G.default_tile(dt, N, K, width)
+            tile = names[ti]
+            d = Dev(G, local, torch)
+            X, XS = d.upload(ops.X(dtype)), d.upload(ops.xscale(dtype))
+            Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
+            assert w == width
+            W, WS = d.upload(Wsh), d.upload(wsc)
+            Y = d.zeros(N * width * 4)
+            wsb = G.workspace_size(dt, ti, N, K, width)
+            WSP = d.zeros(wsb) if wsb else None
+            G.run(local, dt, ti, X, W, Y, N, K, width, XS, WS, WSP, wsb)
+            G.sync(local)
+            host = d.download(Y, np.empty((N, width), np.int32 if dtype == "i8i8" else np.float32))
+            ok, rel = check_rows_of(ops, dtype, host, parity_rows(N), m0, width)
+            with clk.window() as win:
+                ms = G.time(local, dt, ti, X, [W], Y, N, K, width, xscale=XS,
+                            wscales=[WS] if WS is not None else None, workspace=WSP, workspace_bytes=wsb,
+                            warmup=3, iters=iters, flush=FL, flush_bytes=FLUSH_BYTES)
+            windows.append((win.t0, win.t1))
+            med = statistics.median(ms)
+            del d, X, XS, W, WS, Y, WSP
+        except Exception as e:   # reported in the row; the collective below still runs
+            ok, err = False, (str(e).splitlines() or [type(e).__name__])[0][:200]
+        t = torch.tensor([med, rel if ok else float("inf"), 0.0 if ok else 1.0],
+                         dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        med_max, rel_max, bad = (float(v) for v in t.tolist())
+        kind = F.TC_KIND[dtype]
+        peak = bf16 * KIND_RATIO[kind]
+        value = 2.0 * N * K * M / (med_max / 1e3) / 1e12 if med_max < float("inf") else None
+        row = {"shape": "fat", "dtype": dtype, "N": N, "K": K, "M": M, "tile": tile, "width": width,
+               "ms_median_max_over_ranks": med_max, "iters": iters, "value": value, "unit": unit_of(dtype),
+               "kind": kind, "frac_per_gpu": (value / (world * peak)) if value else None,
+               "peak_per_gpu": peak, "peak_source": f"{src} bf16 burst x {KIND_RATIO[kind]:g} (dense kind::{kind})",
+               "parity_ok": bad == 0.0, "max_rel": rel_max}
+        if err:
+            row["error_rank_%d" % rank] = err
+        rows.append(row)
+    return rows, windows
+
+
 def e2e_measure(G, dev, dt, ti, ops, dtype, W, WS, Y, WSP, wsb, N, K, width, a, d):
     """Pinned host X in, GEMM of this rank's block, its Y block out, per step."""
     import ctypes
@@ -652,6 +718,19 @@ def ours(a):
         if dist is not None and not a.no_gathers:
             sharded = gathers(a, torch, dist, world, rank, local, ops, dtype, N, K, M)
             sharded.update({"bcast_ms": bcast_ms, "plan": [list(p) for p in plan]})
+        sharded_suite = None
+        if dist is not None and not a.no_suite:
+            srows, swin = run_sharded_suite(G, torch, dist, world, rank, local, clk, FL, bf16, src)
+            sharded_suite = {"rows": srows, "n": len(srows), "gpus": world,
+                             "parity_ok": all(r["parity_ok"] for r in srows),
+                             "what": ("every dtype at the fat shape, M-sharded across the job's GPUs like the "
+                                      "headline (column blocks of 32-column multiples), default tile per block, "
+                                      "L2 flushed before every timed launch; ms = the max over ranks of each "
+                                      "rank's median; value = 2NKM / ms for the whole job; frac_per_gpu = "
+                                      "value / (gpus x the measured per-kind peak); parity: whole rows of every "
+                                      "rank's block against fp64 numpy"),
+                             "clocks": clk.summary(windows=swin)}
+            ok = ok and sharded_suite["parity_ok"]
 
         line = None
         if rank == 0:
@@ -694,6 +773,8 @@ def ours(a):
             }
             if sharded is not None:
                 line["sharded"] = sharded
+            if sharded_suite is not None:
+                line["sharded_suite"] = sharded_suite
         # per-rank clocks of the timed region
         if dist is not None:
             rec = torch.tensor([clocks["sm_mhz"] or 0.0, clocks["sm_min_mhz"] or 0.0,
