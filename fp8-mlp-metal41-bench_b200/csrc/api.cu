@@ -268,11 +268,13 @@ int gemm_default_tile(int dtype, int N, int K, int M) {
     // A16 kinds on the pair tile widen all of W to f16 first: worth it once the
     // per-128-row conversions of the 1-CTA tiles would repeat (N >= 256)
     const bool a16 = dtype == kINT8 || dtype == kFP8 || dtype == kMXFP4;
-    // f4f4 (kind::mxf4, unit scale cells copied once) and mxfp4/f8 (unit X
-    // cells): the two accumulators of 256x224 measure ahead of the one of
-    // 256x256 (f4f4 fat 70.7 against 74.8 us, square 50.2 against 54.3;
-    // mxfp4/f8 0.5-2.7 %); a4 is even, a8 slower there
-    if ((dtype == kF4F4 || dtype == kF8X4) && N >= 256 && tc_supported(dtype, 256, 224, N, K, M))
+    // f4f4 (kind::mxf4, unit scale cells copied once), mxfp4/f8 (unit X
+    // cells) and mxfp4/a4 (a six-stage ring there): the two accumulators of
+    // 256x224 measure ahead of the one of 256x256 (f4f4 fat 70.7 against
+    // 74.8 us, square 50.2 against 54.3; mxfp4/f8 0.5-2.7 %; a4 fat 68.8
+    // against 70.8 us, square even); a8 is slower there
+    if ((dtype == kF4F4 || dtype == kF8X4 || dtype == kMX4X4) && N >= 256 &&
+        tc_supported(dtype, 256, 224, N, K, M))
       return gemm_tile_index("256x224");
     if ((!a16 || N >= 256) && tc_supported(dtype, 256, 256, N, K, M)) return gemm_tile_index("256x256");
     if (tc_supported(dtype, 128, 256, N, K, M)) return gemm_tile_index("128x256");

@@ -71,10 +71,11 @@ def test_layout_rules_and_tile_support():
     for d in ("mxfp4/a4", "mxfp4/a8", "mxfp4/f8"):
         assert G.tile_names()[G.default_tile(F.CODE[d], 8, 4096, 11008)] == "gemv.mma"
         assert G.tile_names()[G.default_tile(F.CODE[d], 2, 4096, 11008)].startswith("gemv.k")
-    # f4f4 and mxfp4/f8 (unit scale cells copied once): two accumulators on 256x224
+    # f4f4, mxfp4/f8 (unit scale cells copied once) and mxfp4/a4: two accumulators on 256x224
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 2048, 4096, 11008)] == "256x224"
     assert G.tile_names()[G.default_tile(F.CODE["mxfp4/f8"], 2048, 4096, 11008)] == "256x224"
-    assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a4"], 2048, 4096, 11008)] == "256x256"
+    assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a4"], 2048, 4096, 11008)] == "256x224"
+    assert G.tile_names()[G.default_tile(F.CODE["mxfp4/a8"], 2048, 4096, 11008)] == "256x256"
     assert G.tile_names()[G.default_tile(F.CODE["f4f4"], 1, 4096, 11008)] == "gemv.k4"
     # [K,M] GEMVs with two or more rows per CTA: at most 2048 K rows per CTA,
     # at least one CTA per SM at N = 2 and three from N = 3 on (f4f4 has no
