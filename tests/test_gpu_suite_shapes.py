@@ -120,3 +120,55 @@ def test_suite_shape_default_tile(gemm, dtype, shape):
     print(f"{what}: max rel {floored:.3g} (floored at 1e-2 rms), unfloored {unfloored:.3g}, "
           f"{frac:.2e} of outputs above 1e-3 unfloored")
     assert floored <= REL_TOL, what
+
+
+@pytest.mark.parametrize("dtype", F.DTYPES)
+def test_fat_row_shard_blocks(gemm, dtype):
+    # The column blocks of the M-sharded fat row (bench.py and mlp_bench.py
+    # under torchrun): the first and last GPU's block at 4 GPUs (2752 columns
+    # each) and at 8 (1376), each on the tile the block picks by default, run
+    # on this GPU.  Each block is a GEMM of its own: X times the block's
+    # slice of W (and of its scale plane), checked on the same rows as above
+    # against the oracle's decode of that slice.
+    from mlpgemm.data import shard_columns
+    from mlpgemm.shard import shard_plan
+    G = gemm
+    ops = _ops("fat")
+    N, K, M = ops.N, ops.K, ops.M
+    dt = F.CODE[dtype]
+    rows = check_rows(N)
+    xs = ops.xscale(dtype)
+    xd = oracle.decode_x(dtype, ops.X(dtype), xs, N, K)[rows] if dtype != "i8i8" else \
+        np.asarray(ops.X(dtype), np.int8).reshape(N, K)[rows].astype(np.float64)
+    X = G.DeviceBuffer(0, ops.X(dtype).nbytes).upload(ops.X(dtype))
+    XS = None if xs is None else G.DeviceBuffer(0, xs.nbytes).upload(xs)
+    for world, rank in ((4, 0), (4, 3), (8, 0), (8, 7)):
+        m0, width = shard_plan(M, world)[rank]
+        Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
+        assert w == width
+        ti = G.default_tile(dt, N, K, width)
+        W = G.DeviceBuffer(0, Wsh.nbytes).upload(Wsh)
+        WS = None if wsc is None else G.DeviceBuffer(0, wsc.nbytes).upload(wsc)
+        Y = G.DeviceBuffer(0, N * width * 4).zero()
+        wsb = G.workspace_size(dt, ti, N, K, width)
+        WSP = G.DeviceBuffer(0, wsb).zero() if wsb else None
+        G.run(0, dt, ti, X, W, Y, N, K, width, XS, WS, WSP, wsb)
+        G.sync(0)
+        out = Y.download(np.empty((N, width), np.int32 if dtype == "i8i8" else np.float32))[rows]
+        what = f"{dtype} GPU {rank} of {world} (columns {m0}..{m0 + width - 1}) tile {G.tile_names()[ti]}"
+        if dtype == "i8i8":
+            wd = np.asarray(Wsh, np.int8).reshape(K, width).astype(np.float64)
+            ref = (xd @ wd).astype(np.int64)
+            assert np.array_equal(out.astype(np.int64), ref), what
+        else:
+            ref = xd @ oracle.decode_w(dtype, Wsh, wsc, K, width)
+            assert np.all(np.isfinite(out)), what
+            floored, unfloored, _ = rel_errors(out, ref)
+            print(f"{what}: max rel {floored:.3g}, unfloored {unfloored:.3g}")
+            assert floored <= REL_TOL, what
+        for b in (W, WS, Y, WSP):
+            if b is not None:
+                b.close()
+    X.close()
+    if XS is not None:
+        XS.close()
