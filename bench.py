@@ -522,6 +522,7 @@ def run_sharded_suite(G, torch, dist, world, rank, local, clk, FL, bf16, src, it
     block are checked against an fp64 numpy dot product.  Every rank takes the
     same single all-reduce per dtype whatever happened on it, so an error on
     one rank is reported in the row instead of leaving the others waiting."""
+    from mlpgemm import dist_util as DU
     from mlpgemm import formats as F
     from mlpgemm.data import Operands, shard_columns
     from mlpgemm.shard import shard_plan
@@ -530,46 +531,42 @@ def run_sharded_suite(G, torch, dist, world, rank, local, clk, FL, bf16, src, it
     m0, width = plan[rank]
     names = G.tile_names()
     ops = Operands(N, K, M, "seeded", 0)
-    rows, windows = [], []
-    for dtype in F.DTYPES:
+    windows, tiles = [], {}
+
+    def measure(dtype):
         dt = F.CODE[dtype]
-        med, ok, rel, err, tile = float("inf"), False, float("inf"), "", ""
-        try:
-            ti = G.default_tile(dt, N, K, width)
-            tile = names[ti]
-            d = Dev(G, local, torch)
-            X, XS = d.upload(ops.X(dtype)), d.upload(ops.xscale(dtype))
-            Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
-            assert w == width
-            W, WS = d.upload(Wsh), d.upload(wsc)
-            Y = d.zeros(N * width * 4)
-            wsb = G.workspace_size(dt, ti, N, K, width)
-            WSP = d.zeros(wsb) if wsb else None
-            G.run(local, dt, ti, X, W, Y, N, K, width, XS, WS, WSP, wsb)
-            G.sync(local)
-            host = d.download(Y, np.empty((N, width), np.int32 if dtype == "i8i8" else np.float32))
-            ok, rel = check_rows_of(ops, dtype, host, parity_rows(N), m0, width)
-            with clk.window() as win:
-                ms = G.time(local, dt, ti, X, [W], Y, N, K, width, xscale=XS,
-                            wscales=[WS] if WS is not None else None, workspace=WSP, workspace_bytes=wsb,
-                            warmup=3, iters=iters, flush=FL, flush_bytes=FLUSH_BYTES)
-            windows.append((win.t0, win.t1))
-            med = statistics.median(ms)
-            del d, X, XS, W, WS, Y, WSP
-        except Exception as e:   # reported in the row; the collective below still runs
-            ok, err = False, (str(e).splitlines() or [type(e).__name__])[0][:200]
-        t = torch.tensor([med, rel if ok else float("inf"), 0.0 if ok else 1.0],
-                         dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        med_max, rel_max, bad = (float(v) for v in t.tolist())
+        ti = G.default_tile(dt, N, K, width)
+        tiles[dtype] = names[ti]
+        d = Dev(G, local, torch)
+        X, XS = d.upload(ops.X(dtype)), d.upload(ops.xscale(dtype))
+        Wsh, wsc, _, w = shard_columns(ops, dtype, rank, world)
+        assert w == width
+        W, WS = d.upload(Wsh), d.upload(wsc)
+        Y = d.zeros(N * width * 4)
+        wsb = G.workspace_size(dt, ti, N, K, width)
+        WSP = d.zeros(wsb) if wsb else None
+        G.run(local, dt, ti, X, W, Y, N, K, width, XS, WS, WSP, wsb)
+        G.sync(local)
+        host = d.download(Y, np.empty((N, width), np.int32 if dtype == "i8i8" else np.float32))
+        ok, rel = check_rows_of(ops, dtype, host, parity_rows(N), m0, width)
+        with clk.window() as win:
+            ms = G.time(local, dt, ti, X, [W], Y, N, K, width, xscale=XS,
+                        wscales=[WS] if WS is not None else None, workspace=WSP, workspace_bytes=wsb,
+                        warmup=3, iters=iters, flush=FL, flush_bytes=FLUSH_BYTES)
+        windows.append((win.t0, win.t1))
+        return statistics.median(ms), ok, rel
+
+    rows = []
+    for dtype, (ms_max, rel_max, ok, err) in zip(F.DTYPES, DU.reduce_rows(dist, f"cuda:{local}", F.DTYPES,
+                                                                          measure)):
         kind = F.TC_KIND[dtype]
         peak = bf16 * KIND_RATIO[kind]
-        value = 2.0 * N * K * M / (med_max / 1e3) / 1e12 if med_max < float("inf") else None
-        row = {"shape": "fat", "dtype": dtype, "N": N, "K": K, "M": M, "tile": tile, "width": width,
-               "ms_median_max_over_ranks": med_max, "iters": iters, "value": value, "unit": unit_of(dtype),
-               "kind": kind, "frac_per_gpu": (value / (world * peak)) if value else None,
+        value = 2.0 * N * K * M / (ms_max / 1e3) / 1e12 if ms_max < float("inf") else None
+        row = {"shape": "fat", "dtype": dtype, "N": N, "K": K, "M": M, "tile": tiles.get(dtype, ""),
+               "width": width, "ms_median_max_over_ranks": ms_max, "iters": iters, "value": value,
+               "unit": unit_of(dtype), "kind": kind, "frac_per_gpu": (value / (world * peak)) if value else None,
                "peak_per_gpu": peak, "peak_source": f"{src} bf16 burst x {KIND_RATIO[kind]:g} (dense kind::{kind})",
-               "parity_ok": bad == 0.0, "max_rel": rel_max}
+               "parity_ok": ok, "max_rel": rel_max}
         if err:
             row["error_rank_%d" % rank] = err
         rows.append(row)

@@ -30,3 +30,26 @@ def weak_scaling_rate(work_per_rank: float, world: int, steps: int, max_total_ms
 def strong_scaling_rate(total_work: float, max_median_ms: float) -> float:
     """Rate of one GEMM split across ranks: total work / slowest rank."""
     return total_work / (max_median_ms / 1e3) / 1e12
+
+
+def reduce_rows(dist, device, keys, measure):
+    """Per key, this rank's measure(key) -> (median ms, parity ok, max rel),
+    then one all-reduce (max) of [ms, rel, failed] over the ranks, taken
+    whatever happened on this rank: an exception in measure counts as a
+    failed row with an infinite time, so the other ranks are never left
+    waiting in a collective that this rank skipped.  Returns, per key, the
+    job's (max ms, max rel, every rank ok, this rank's error text or "")."""
+    import torch
+    out = []
+    for key in keys:
+        ms, ok, rel, err = float("inf"), False, float("inf"), ""
+        try:
+            ms, ok, rel = measure(key)
+        except Exception as e:   # reported in the row; the collective below still runs
+            ok, err = False, (str(e).splitlines() or [type(e).__name__])[0][:200]
+        t = torch.tensor([float(ms), float(rel) if ok else float("inf"), 0.0 if ok else 1.0],
+                         dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max, rel_max, failed = (float(v) for v in t.tolist())
+        out.append((ms_max, rel_max, failed == 0.0, err))
+    return out

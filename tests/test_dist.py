@@ -49,6 +49,41 @@ def test_two_gloo_ranks_aggregate():
         assert rate == pytest.approx(2.0 * 4096 ** 3 * 2 * 100 / 0.015 / 1e12)
 
 
+def _rows_reduce_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        def measure(key):
+            if key == "a":                      # both ranks fine: the job takes the slower
+                return 1.0 + rank, True, 1e-4 * (rank + 1)
+            if key == "b" and rank == 1:        # this rank's run fails outright
+                raise RuntimeError("boom on rank 1\nsecond line")
+            if key == "c" and rank == 0:        # this rank's parity check fails
+                return 0.5, False, 0.25
+            return 0.5, True, 0.0
+        out[rank] = DU.reduce_rows(dist, "cpu", ["a", "b", "c", "d"], measure)
+        dist.barrier()   # every rank reached here: no collective was skipped
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_reduce_rows_with_a_failing_rank():
+    # the per-dtype rows of bench.py's sharded suite: one all-reduce per row
+    # on every rank, even where one rank's run raised or failed its check
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_rows_reduce_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    inf = float("inf")
+    for r in range(world):
+        a, b, c, d = out[r]
+        assert a == (2.0, 2e-4, True, "")
+        assert b[:3] == (inf, inf, False)
+        assert b[3] == ("boom on rank 1" if r == 1 else "")
+        assert c[:3] == (0.5, inf, False) and c[3] == ""
+        assert d == (0.5, 0.0, True, "")
+
+
 def test_shard_plan_covers_columns():
     for M in (4096, 11008, 1000, 33):
         for G in (1, 2, 4, 8):
